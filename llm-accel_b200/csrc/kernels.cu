@@ -1,0 +1,665 @@
+// sm_100a kernels of the resident decoder-layer path (Task 18 / 19 / 20).
+//
+// Projections (kernel/mm_stream_8x64_fused_mac.cpp:138-205 + the conversion of
+// kernel/compute_core_8x64_unified.cpp:10-39) become one weight-streaming
+// kernel: each warp owns a pair of output rows, streams both rows once from HBM
+// with 128-bit loads and forms exact int16 x int16 dot products with the
+// integer dp2a pipe (weights pre-split into signed high / unsigned low bytes,
+// activations packed as int16 pairs), so every MAC is exact and reduction order
+// is free.  The rounding epilogue of the MAC engine is fused with what follows
+// the projection in the controller's schedule: RoPE + KV append (Q/K/V),
+// residual add (O, Down), SiLU x Up (Gate/Up), or an int64 export for the
+// tensor-parallel all-reduce.  RMSNorm (kernel/compute_stream.cpp:227-288) is
+// the prologue that stages the activations in shared memory.
+//
+// Attention (run_cc8_resident_decode_attention kernel/control_cache_8x64.cpp:5492-5765)
+// keeps the reference's 64-position tile recurrence bit-exact while running
+// tiles in parallel: pass 1 writes per-tile QK scores and tile maxima; pass 2
+// recomputes the running max of each tile as a prefix max, produces the tile's
+// Q2.14 probabilities, tile sum and PV tile value, and the last CTA of a
+// (row, KV head) replays the cheap Q16.16 rescale/accumulate recurrence over
+// tiles in order and finalises.  Scores never leave L2-sized scratch.
+#include <cuda_runtime.h>
+
+#include "fixed.cuh"
+#include "kernels.cuh"
+
+namespace llmx {
+
+// --------------------------------------------------------------------------
+// small device helpers
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// a: two signed int16 (low half = even k); b: bytes; .lo uses bytes 0,1 (unsigned)
+__device__ __forceinline__ int dp2a_lo_su(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// .hi uses bytes 2,3 (signed)
+__device__ __forceinline__ int dp2a_hi_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int32_t add_sat(int32_t a, int32_t b) {
+    int32_t d;
+    asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ int64_t shfl_xor64(int64_t v, int o) {
+    return __shfl_xor_sync(0xffffffffu, v, o);
+}
+
+// golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
+// then x up with one rounding (stream_silu_mul :123-164).
+__device__ __forceinline__ int32_t silu_mul(int32_t g, int32_t u, const int16_t *__restrict__ etab) {
+    int32_t s;
+    if (g >= 0) {
+        const int32_t idx = -g < -2048 ? 0 : 2048 - g;
+        const int32_t e = __ldg(etab + idx);
+        const int32_t r = recip_q88(sat16(256 + e));
+        s = sat16(rnd((int64_t)g * r, 8));
+    } else {
+        const int32_t idx = g < -2048 ? 0 : g + 2048;
+        const int32_t e = __ldg(etab + idx);
+        const int32_t r = recip_q88(sat16(256 + e));
+        s = sat16(rnd((int64_t)g * e * r, 16));
+    }
+    return sat16(rnd((int64_t)s * u, 8));
+}
+
+// Halving ("transpose") warp reduction of N int64 values: afterwards lane L
+// holds the warp total of value index idx(L); lanes differing only in bits
+// below 32/N hold the same index.  N <= 16.
+template <int N>
+__device__ __forceinline__ int64_t warp_reduce_n(int64_t (&v)[N], int lane, int &idx) {
+    idx = 0;
+#pragma unroll
+    for (int n = N, o = 16; n > 1; n >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) {
+            const int64_t send = up ? v[i] : v[i + n / 2];
+            const int64_t keep = up ? v[i + n / 2] : v[i];
+            v[i] = keep + shfl_xor64(send, o);
+        }
+        if (up) idx += n / 2;
+    }
+    int64_t t = v[0];
+#pragma unroll
+    for (int o = 16 / N; o >= 1; o >>= 1) t += shfl_xor64(t, o);
+    return t;
+}
+
+// --------------------------------------------------------------------------
+// activation prologue: rows -> shared memory (optionally RMS-normalised)
+// --------------------------------------------------------------------------
+template <int R>
+__device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows) {
+    const int K = a.K;
+    const int KV8 = K >> 3;
+    uint4 *xs4 = reinterpret_cast<uint4 *>(xs);
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
+    __shared__ int32_t inv_rms_s[kMaxRows];
+    if (a.norm != nullptr) {
+        if (a.inv_elems == 0) {
+            // recip(fm(K)) == 0: mean == 0 for every input, inv_rms is a constant.
+            if (threadIdx.x < R) inv_rms_s[threadIdx.x] = a.inv_rms_const;
+        } else {
+            __shared__ int64_t red[kWarps][kMaxRows];
+            int64_t part[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) part[r] = 0;
+            for (int i = threadIdx.x; i < K; i += blockDim.x) {
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (r < rows) {
+                        const int32_t v = a.x[(size_t)r * K + i];
+                        part[r] += (int64_t)v * v;
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) part[r] += shfl_xor64(part[r], o);
+            }
+            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < R; r++) red[warp][r] = part[r];
+            }
+            __syncthreads();
+            if (threadIdx.x < R) {
+                int64_t s = 0;
+                for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w][threadIdx.x];
+                // saturating running sum == min(total, INT32_MAX) since terms are >= 0
+                const int32_t sum = s > INT32_MAX ? INT32_MAX : (int32_t)s;
+                inv_rms_s[threadIdx.x] = inv_rms_q88(sum, a.inv_elems);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < R * K; i += blockDim.x) {
+            const int r = i / K, e = i - r * K;
+            int32_t y = 0;
+            if (r < rows) {
+                const int64_t p = (int64_t)a.x[(size_t)r * K + e] * inv_rms_s[r] * a.norm[e];
+                y = sat16(rnd(p, 16));
+            }
+            xs[i] = (int16_t)y;
+        }
+    } else {
+        for (int i = threadIdx.x; i < R * KV8; i += blockDim.x) {
+            const int r = i / KV8;
+            xs4[i] = r < rows ? x4[i] : make_uint4(0, 0, 0, 0);
+        }
+    }
+    __syncthreads();
+}
+
+// --------------------------------------------------------------------------
+// projection kernel
+// --------------------------------------------------------------------------
+template <int R, int EPI>
+__global__ void __launch_bounds__(kWarps * 32) k_proj(const ProjArgs a) {
+    extern __shared__ __align__(16) int16_t xs[];
+    constexpr int N = 2 * R;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = a.K, KV8 = K >> 3;
+    const int nchunks = (KV8 + 255) >> 8;
+    const int nw = gridDim.x * kWarps;
+    int p = blockIdx.x * kWarps + warp;
+
+    uint4 wa[8], wb[8];
+    auto load_chunk = [&](int pair, int c) {
+        const uint4 *base = reinterpret_cast<const uint4 *>(a.w + (size_t)pair * K);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int v = (c << 8) + (j << 5) + lane;
+            if (v < KV8) {
+                wa[j] = ld_stream(base + v);
+                wb[j] = ld_stream(base + KV8 + v);
+            } else {
+                wa[j] = make_uint4(0, 0, 0, 0);
+                wb[j] = make_uint4(0, 0, 0, 0);
+            }
+        }
+    };
+
+    // Weights do not depend on the producer kernel: start streaming them
+    // before waiting for it (programmatic dependent launch).
+    bool preloaded = p < a.npairs;
+    if (preloaded) load_chunk(p, 0);
+    pdl_trigger();
+    pdl_wait();
+    const Step st = *a.step;
+    const int rows = st.rows;
+    stage_rows<R>(a, xs, rows);
+    const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
+
+    for (; p < a.npairs; p += nw) {
+        int64_t acc[N];
+#pragma unroll
+        for (int i = 0; i < N; i++) acc[i] = 0;
+        for (int c = 0; c < nchunks; c++) {
+            if (c > 0 || !preloaded) load_chunk(p, c);
+            int lo[N], hi[N];
+#pragma unroll
+            for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int v = (c << 8) + (j << 5) + lane;
+                if (v < KV8) {
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        const uint4 x = xs4[r * KV8 + v];
+                        lo[2 * r] = dp2a_lo_su(x.x, wa[j].x, lo[2 * r]);
+                        hi[2 * r] = dp2a_hi_ss(x.x, wa[j].x, hi[2 * r]);
+                        lo[2 * r] = dp2a_lo_su(x.y, wa[j].y, lo[2 * r]);
+                        hi[2 * r] = dp2a_hi_ss(x.y, wa[j].y, hi[2 * r]);
+                        lo[2 * r] = dp2a_lo_su(x.z, wa[j].z, lo[2 * r]);
+                        hi[2 * r] = dp2a_hi_ss(x.z, wa[j].z, hi[2 * r]);
+                        lo[2 * r] = dp2a_lo_su(x.w, wa[j].w, lo[2 * r]);
+                        hi[2 * r] = dp2a_hi_ss(x.w, wa[j].w, hi[2 * r]);
+                        lo[2 * r + 1] = dp2a_lo_su(x.x, wb[j].x, lo[2 * r + 1]);
+                        hi[2 * r + 1] = dp2a_hi_ss(x.x, wb[j].x, hi[2 * r + 1]);
+                        lo[2 * r + 1] = dp2a_lo_su(x.y, wb[j].y, lo[2 * r + 1]);
+                        hi[2 * r + 1] = dp2a_hi_ss(x.y, wb[j].y, hi[2 * r + 1]);
+                        lo[2 * r + 1] = dp2a_lo_su(x.z, wb[j].z, lo[2 * r + 1]);
+                        hi[2 * r + 1] = dp2a_hi_ss(x.z, wb[j].z, hi[2 * r + 1]);
+                        lo[2 * r + 1] = dp2a_lo_su(x.w, wb[j].w, lo[2 * r + 1]);
+                        hi[2 * r + 1] = dp2a_hi_ss(x.w, wb[j].w, hi[2 * r + 1]);
+                    }
+                }
+            }
+            // |lo| <= 32 * 2 * 255 * 32768 < 2^29, |hi| <= 32 * 2 * 128 * 32768 = 2^28
+#pragma unroll
+            for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
+        }
+        const int pcur = p;
+        // start streaming the next pair before the reduction and epilogue
+        preloaded = p + nw < a.npairs;
+        if (preloaded) load_chunk(p + nw, 0);
+
+        int idx;
+        const int64_t tot = warp_reduce_n<N>(acc, lane, idx);
+        constexpr int kPartnerBit = 32 / N;
+        const int64_t other = __shfl_sync(0xffffffffu, tot, lane | kPartnerBit);
+        const int r = idx >> 1;
+        if ((lane & (kPartnerBit - 1)) != 0 || (idx & 1) != 0 || r >= rows) continue;
+        if (EPI == EPI_PARTIAL) {
+            a.partial[(size_t)r * (2 * a.npairs) + 2 * pcur] = tot;
+            a.partial[(size_t)r * (2 * a.npairs) + 2 * pcur + 1] = other;
+            continue;
+        }
+        const int32_t y0 = round_mac(tot), y1 = round_mac(other);
+        if (EPI == EPI_RESID) {
+            const size_t o = (size_t)r * a.out_stride + 2 * pcur;
+            a.out[o] = (int16_t)sat16((int32_t)a.resid[o] + y0);
+            a.out[o + 1] = (int16_t)sat16((int32_t)a.resid[o + 1] + y1);
+        } else if (EPI == EPI_SILU) {
+            a.out[(size_t)r * a.out_stride + pcur] = (int16_t)silu_mul(y0, y1, a.etab);
+        } else if (EPI == EPI_QKV) {
+            const int half = a.hd >> 1;
+            const int pos = st.position + r;
+            int pp = pcur;
+            if (pp < a.q_pairs + a.kv_pairs) {
+                // RoPE rotate_fix16_pair_with_quantized_rope host:4765-4788
+                const bool isq = pp < a.q_pairs;
+                if (!isq) pp -= a.q_pairs;
+                const int head = pp / half, i = pp - head * half;
+                const int64_t c = a.rope[(size_t)pos * a.hd + i];
+                const int64_t s = a.rope[(size_t)pos * a.hd + half + i];
+                const int16_t z0 = (int16_t)sat16(rnd((int64_t)y0 * c - (int64_t)y1 * s, 8));
+                const int16_t z1 = (int16_t)sat16(rnd((int64_t)y1 * c + (int64_t)y0 * s, 8));
+                int16_t *dst = isq ? a.out + (size_t)r * a.out_stride + (size_t)head * a.hd
+                                   : a.kc + ((size_t)head * a.max_seq + pos) * a.hd;
+                dst[i] = z0;
+                dst[i + half] = z1;
+            } else {
+                pp -= a.q_pairs + a.kv_pairs;
+                const int head = pp / half, i = pp - head * half;
+                int16_t *dst = a.vc + ((size_t)head * a.max_seq + pos) * a.hd;
+                dst[i] = (int16_t)y0;
+                dst[i + half] = (int16_t)y1;
+            }
+        }
+    }
+}
+
+template <int R, int EPI>
+static cudaError_t launch_proj_t(const ProjArgs &a, int grid, cudaStream_t s) {
+    const size_t smem = (size_t)R * a.K * sizeof(int16_t);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_proj<R, EPI>, a);
+}
+
+template <int EPI>
+static cudaError_t launch_proj_r(const ProjArgs &a, int rows_tmpl, int grid, cudaStream_t s) {
+    switch (rows_tmpl) {
+    case 1: return launch_proj_t<1, EPI>(a, grid, s);
+    case 2: return launch_proj_t<2, EPI>(a, grid, s);
+    case 4: return launch_proj_t<4, EPI>(a, grid, s);
+    default: return launch_proj_t<8, EPI>(a, grid, s);
+    }
+}
+
+cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s) {
+    switch (epi) {
+    case EPI_QKV: return launch_proj_r<EPI_QKV>(a, rows_tmpl, grid, s);
+    case EPI_RESID: return launch_proj_r<EPI_RESID>(a, rows_tmpl, grid, s);
+    case EPI_SILU: return launch_proj_r<EPI_SILU>(a, rows_tmpl, grid, s);
+    default: return launch_proj_r<EPI_PARTIAL>(a, rows_tmpl, grid, s);
+    }
+}
+
+size_t proj_smem_bytes(int rows_tmpl, int K) { return (size_t)rows_tmpl * K * sizeof(int16_t); }
+
+template <int EPI>
+static cudaError_t configure_epi(int bytes) {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_proj<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_proj<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_proj<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    return cudaFuncSetAttribute(k_proj<8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// Opt every projection instantiation into large dynamic shared memory on the
+// current device (8 rows x 11008 inputs = 172 KiB for the Down projection).
+cudaError_t proj_configure(int max_smem_bytes) {
+    cudaError_t e;
+    if ((e = configure_epi<EPI_QKV>(max_smem_bytes))) return e;
+    if ((e = configure_epi<EPI_RESID>(max_smem_bytes))) return e;
+    if ((e = configure_epi<EPI_SILU>(max_smem_bytes))) return e;
+    return configure_epi<EPI_PARTIAL>(max_smem_bytes);
+}
+
+template <int R, int EPI>
+static int occ_t(int K) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_proj<R, EPI>, kWarps * 32,
+                                                  (size_t)R * K * sizeof(int16_t));
+    return n;
+}
+int proj_max_ctas_per_sm(int epi, int rows_tmpl, int K) {
+    // all epilogues share the register/smem profile closely enough; use RESID
+    (void)epi;
+    switch (rows_tmpl) {
+    case 1: return occ_t<1, EPI_RESID>(K);
+    case 2: return occ_t<2, EPI_RESID>(K);
+    case 4: return occ_t<4, EPI_RESID>(K);
+    default: return occ_t<8, EPI_RESID>(K);
+    }
+}
+
+// --------------------------------------------------------------------------
+// attention pass 1: QK scores of one 64-position tile for the query heads of
+// one KV head (golden_attention_mm host:3219-3278 with scale_qk)
+// --------------------------------------------------------------------------
+constexpr int kKvStride = 136;  // padded smem row (int16) -> conflict-free 128-bit reads
+constexpr int kAttnThreads = 256;
+constexpr int kMaxHd = 128;
+constexpr int kMaxGroup = 8;
+
+__global__ void __launch_bounds__(kAttnThreads) k_attn_scores(const AttnArgs a) {
+    __shared__ __align__(16) int16_t ks[kTile * kKvStride];
+    __shared__ __align__(16) int16_t qs[kMaxGroup * kMaxHd];
+    __shared__ int32_t hmax[kMaxGroup][kAttnThreads / 32];
+    pdl_trigger();
+    pdl_wait();
+    const Step st = *a.step;
+    const int r = blockIdx.z, slot = blockIdx.y, t = blockIdx.x;
+    if (r >= st.rows) return;
+    const int ctx = st.position + r + 1;
+    const int ntiles = (ctx + kTile - 1) / kTile;
+    if (t >= ntiles) return;
+    const int p0 = t * kTile;
+    const int tl = min(kTile, ctx - p0);
+    const int hd = a.hd, G = a.group;
+    const int kvh = a.kv_first + slot;  // KV heads are replicated on every rank
+    const int16_t *kbase = a.kc + ((size_t)kvh * a.max_seq + p0) * hd;
+    // K tile -> Q4.12 with saturation (golden_weight_t(fm))
+    for (int i = threadIdx.x; i < tl * hd; i += blockDim.x) {
+        const int p = i / hd, e = i - p * hd;
+        ks[p * kKvStride + e] = (int16_t)sat16((int32_t)kbase[(size_t)p * hd + e] * 16);
+    }
+    const int16_t *qbase = a.q + (size_t)r * a.q_heads * hd + (size_t)slot * G * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qbase[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int32_t local_max[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; h++) local_max[h] = -32768;
+    for (int i = threadIdx.x; i < G * kTile; i += blockDim.x) {
+        const int h = i / kTile, p = i - h * kTile;
+        if (p >= tl) continue;
+        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+        const int16_t *qv = qs + h * hd;
+        const int16_t *kv = ks + p * kKvStride;
+        for (int e = 0; e < hd; e += 4) {
+            // per-product rounding to Q16.16, four saturating banks (k mod 4)
+            b0 = add_sat(b0, (int32_t)rnd((int32_t)qv[e] * (int32_t)kv[e], 4));
+            b1 = add_sat(b1, (int32_t)rnd((int32_t)qv[e + 1] * (int32_t)kv[e + 1], 4));
+            b2 = add_sat(b2, (int32_t)rnd((int32_t)qv[e + 2] * (int32_t)kv[e + 2], 4));
+            b3 = add_sat(b3, (int32_t)rnd((int32_t)qv[e + 3] * (int32_t)kv[e + 3], 4));
+        }
+        int32_t tot = sat32((int64_t)b0 + b1 + b2 + b3);
+        tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));
+        const int32_t sc = sat16(rnd(tot, 8));
+        a.scores[((size_t)r * a.q_heads + slot * G + h) * a.max_seq + p0 + p] = (int16_t)sc;
+#pragma unroll
+        for (int hh = 0; hh < kMaxGroup; hh++)
+            if (hh == h) local_max[hh] = max(local_max[hh], sc);
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; h++) {
+        int32_t m = local_max[h];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) hmax[h][warp] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        int32_t m = -32768;
+        for (int w = 0; w < kAttnThreads / 32; w++) m = max(m, hmax[threadIdx.x][w]);
+        a.tmax[((size_t)r * a.q_heads + slot * G + threadIdx.x) * a.max_tiles + t] = (int16_t)m;
+    }
+}
+
+// --------------------------------------------------------------------------
+// attention pass 2: probabilities, tile sum, PV of one tile; the last CTA of
+// a (row, KV head) combines the tiles in order and finalises
+// (golden_tiled_flash_attention_q2_14_impl<true> host:3610-3739)
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(kAttnThreads) k_attn_pv(const AttnArgs a) {
+    __shared__ __align__(16) int16_t vs[kTile * kKvStride];
+    __shared__ int16_t ps[kMaxGroup][kTile];
+    __shared__ int32_t mcur[kMaxGroup], mprev[kMaxGroup];
+    __shared__ int32_t tsum_s[kMaxGroup];
+    __shared__ uint32_t ticket_s;
+    pdl_trigger();
+    pdl_wait();
+    const Step st = *a.step;
+    const int r = blockIdx.z, slot = blockIdx.y, t = blockIdx.x;
+    if (r >= st.rows) return;
+    const int ctx = st.position + r + 1;
+    const int ntiles = (ctx + kTile - 1) / kTile;
+    if (t >= ntiles) return;
+    const int p0 = t * kTile;
+    const int tl = min(kTile, ctx - p0);
+    const int hd = a.hd, G = a.group;
+    const size_t hrow = (size_t)r * a.q_heads + (size_t)slot * G;  // first local head row
+
+    if (threadIdx.x < G) {
+        // running max after tile t and before it (m_{-1} = fm(-128))
+        const int16_t *tm = a.tmax + (hrow + threadIdx.x) * a.max_tiles;
+        int32_t mp = -32768;
+        for (int u = 0; u < t; u++) mp = max(mp, (int32_t)tm[u]);
+        mprev[threadIdx.x] = mp;
+        mcur[threadIdx.x] = max(mp, (int32_t)tm[t]);
+    }
+    const int16_t *vbase = a.vc + ((size_t)(a.kv_first + slot) * a.max_seq + p0) * hd;
+    for (int i = threadIdx.x; i < tl * hd; i += blockDim.x) {
+        const int p = i / hd, e = i - p * hd;
+        vs[p * kKvStride + e] = (int16_t)sat16((int32_t)vbase[(size_t)p * hd + e] * 16);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kTile; i += blockDim.x) {
+        const int h = i / kTile, p = i - h * kTile;
+        int32_t pr = 0;
+        if (p < tl) {
+            const int32_t s = a.scores[(hrow + h) * a.max_seq + p0 + p];
+            int32_t d = sat16(s - mcur[h]);
+            d = d < -2048 ? -2048 : (d > 0 ? 0 : d);
+            pr = __ldg(a.ptab + d + 2048);
+        }
+        ps[h][p] = (int16_t)pr;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        int32_t ts = 0;
+        for (int p = 0; p < tl; p++) ts = add_sat(ts, (int32_t)ps[threadIdx.x][p] * 4);
+        tsum_s[threadIdx.x] = ts;
+        int32_t d = sat16(mprev[threadIdx.x] - mcur[threadIdx.x]);
+        d = d < -2048 ? -2048 : d;
+        const size_t ti = (hrow + threadIdx.x) * a.max_tiles + t;
+        a.tsum[ti] = ts;
+        a.told[ti] = __ldg(a.ptab + d + 2048);
+    }
+    // PV with the raw-payload semantics: payload raw p read as Q8.8 times
+    // V as Q4.12 (saturated) rounded to Q16.16 per product, four banks
+    // (never saturate: |p*v| <= 2^29), x accum(fm(1/64)), -> fm.
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int h = i / hd, e = i - h * hd;
+        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+        int p = 0;
+        for (; p + 3 < tl; p += 4) {
+            b0 += (int32_t)rnd((int32_t)ps[h][p] * (int32_t)vs[p * kKvStride + e], 4);
+            b1 += (int32_t)rnd((int32_t)ps[h][p + 1] * (int32_t)vs[(p + 1) * kKvStride + e], 4);
+            b2 += (int32_t)rnd((int32_t)ps[h][p + 2] * (int32_t)vs[(p + 2) * kKvStride + e], 4);
+            b3 += (int32_t)rnd((int32_t)ps[h][p + 3] * (int32_t)vs[(p + 3) * kKvStride + e], 4);
+        }
+        if (p < tl) b0 += (int32_t)rnd((int32_t)ps[h][p] * (int32_t)vs[p * kKvStride + e], 4);
+        if (p + 1 < tl) b1 += (int32_t)rnd((int32_t)ps[h][p + 1] * (int32_t)vs[(p + 1) * kKvStride + e], 4);
+        if (p + 2 < tl) b2 += (int32_t)rnd((int32_t)ps[h][p + 2] * (int32_t)vs[(p + 2) * kKvStride + e], 4);
+        int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
+        ts = sat32(rnd((int64_t)ts * 1024, 16));
+        a.tval[((hrow + h) * a.max_tiles + t) * hd + e] = (int16_t)sat16(rnd(ts, 8));
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ticket_s = atomicAdd(a.tickets + (size_t)r * gridDim.y + slot, 1u);
+    __syncthreads();
+    if (ticket_s != (uint32_t)(ntiles - 1)) return;
+    __threadfence();
+    // sequential Q16.16 recurrence over the tiles, in order
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int h = i / hd, e = i - h * hd;
+        const size_t hb = (hrow + h) * a.max_tiles;
+        int32_t sum = 0, acc = 0;
+        for (int u = 0; u < ntiles; u++) {
+            const int64_t old = (int64_t)__ldcg(a.told + hb + u) * 4;  // Q2.14 -> Q16.16
+            sum = sat32(rnd((int64_t)sum * old, 16) + __ldcg(a.tsum + hb + u));
+            acc = sat32(rnd((int64_t)acc * old, 16));
+            acc = sat32((int64_t)acc + (int64_t)__ldcg(a.tval + (hb + u) * hd + e) * 256);
+        }
+        const int64_t safe = sum < 16 ? 16 : sum;
+        const int64_t quot = ((int64_t)1 << 32) / safe;  // accum(1)/safe, 16 fraction bits
+        const int64_t inv = sat16(rnd(quot, 8));
+        a.out[(size_t)r * a.q_heads * hd + (size_t)(slot * G + h) * hd + e] =
+            (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
+    }
+    if (threadIdx.x == 0) a.tickets[(size_t)r * gridDim.y + slot] = 0;
+}
+
+static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t launch_attn_scores(const AttnArgs &a, int rows, cudaStream_t s) {
+    AttnArgs c = a;
+    void *args[] = {&c};
+    return launch_pdl((const void *)k_attn_scores, dim3(a.max_tiles, a.q_heads / a.group, rows),
+                      dim3(kAttnThreads), args, s);
+}
+
+cudaError_t launch_attn_pv(const AttnArgs &a, int rows, cudaStream_t s) {
+    AttnArgs c = a;
+    void *args[] = {&c};
+    return launch_pdl((const void *)k_attn_pv, dim3(a.max_tiles, a.q_heads / a.group, rows),
+                      dim3(kAttnThreads), args, s);
+}
+
+// --------------------------------------------------------------------------
+// Task 20: final RMSNorm of 1..8 rows (stream_rmsnorm compute_stream.cpp:227-288)
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_rmsnorm(const NormArgs a) {
+    __shared__ int64_t red[8];
+    __shared__ int32_t inv_s;
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x;
+    if (r >= a.step->rows) return;
+    const int16_t *x = a.x + (size_t)r * a.n;
+    if (a.inv_elems == 0) {
+        if (threadIdx.x == 0) inv_s = a.inv_rms_const;
+    } else {
+        int64_t part = 0;
+        for (int i = threadIdx.x; i < a.n; i += blockDim.x) part += (int64_t)x[i] * x[i];
+        for (int o = 16; o >= 1; o >>= 1) part += shfl_xor64(part, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int64_t s = 0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+            inv_s = inv_rms_q88(s > INT32_MAX ? INT32_MAX : (int32_t)s, a.inv_elems);
+        }
+    }
+    __syncthreads();
+    const int64_t inv = inv_s;
+    for (int i = threadIdx.x; i < a.n; i += blockDim.x)
+        a.y[(size_t)r * a.n + i] = (int16_t)sat16(rnd((int64_t)x[i] * inv * a.w[i], 16));
+}
+
+cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s) {
+    NormArgs c = a;
+    void *args[] = {&c};
+    return launch_pdl((const void *)k_rmsnorm, dim3(rows), dim3(256), args, s);
+}
+
+// --------------------------------------------------------------------------
+// tensor parallel: round the all-reduced exact sums and add the residual
+// --------------------------------------------------------------------------
+__global__ void k_round_resid(const ResidArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int rows = a.step->rows;
+    const int total = rows * a.n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x)
+        a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(a.partial[i]));
+}
+
+cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {
+    ResidArgs c = a;
+    void *args[] = {&c};
+    const int blocks = (rows * a.n + 255) / 256;
+    return launch_pdl((const void *)k_round_resid, dim3(blocks), dim3(256), args, s);
+}
+
+// --------------------------------------------------------------------------
+// weight layout
+// --------------------------------------------------------------------------
+__global__ void k_pack_pairs(const int16_t *__restrict__ dense, int ld, int col0, int K,
+                             const int32_t *__restrict__ row_of_slot, int nslots,
+                             uint32_t *__restrict__ dst) {
+    const int KW = K >> 1;
+    const size_t total = (size_t)nslots * KW;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int slot = (int)(i / KW);
+        const int j = (int)(i - (size_t)slot * KW);
+        const int16_t *row = dense + (size_t)row_of_slot[slot] * ld + col0;
+        const uint32_t w0 = (uint16_t)row[2 * j], w1 = (uint16_t)row[2 * j + 1];
+        dst[i] = (w0 & 0xffu) | ((w1 & 0xffu) << 8) | ((w0 >> 8) << 16) | ((w1 >> 8) << 24);
+    }
+}
+
+cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
+                              const int32_t *row_of_slot, int nslots, uint32_t *dst,
+                              cudaStream_t s) {
+    const size_t total = (size_t)nslots * (K >> 1);
+    int blocks = (int)((total + 255) / 256);
+    if (blocks > 65535 * 8) blocks = 65535 * 8;
+    k_pack_pairs<<<blocks, 256, 0, s>>>(dense, ld, col0, K, row_of_slot, nslots, dst);
+    return cudaGetLastError();
+}
+
+}  // namespace llmx

@@ -1,0 +1,109 @@
+// Kernel argument blocks and launch entry points of the resident layer path.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace llmx {
+
+constexpr int kTile = 64;     // online-softmax tile: include/control_cache_8x64.hpp:72
+constexpr int kMaxRows = 8;   // kMaxTokensPerLaunch host:38
+constexpr int kWarps = 8;     // warps per CTA of the projection kernels
+
+// Position/row count of the running task, read by every kernel from device
+// memory so that one captured graph serves every position.
+struct Step {
+    int32_t position;
+    int32_t rows;
+};
+
+enum Epi : int {
+    EPI_QKV = 0,   // RoPE on Q/K, Q -> q buffer, K/V -> KV cache
+    EPI_RESID = 1, // + residual -> hidden out (O and Down projections)
+    EPI_SILU = 2,  // gate/up pair -> SiLU(g)*u -> FFN activation
+    EPI_PARTIAL = 3 // exact int64 partial sums (tensor-parallel ranks)
+};
+
+struct ProjArgs {
+    const uint32_t *w;   // pair-interleaved, byte-split weights (see layout.cu)
+    int K;               // input features
+    int npairs;          // output row pairs
+    const int16_t *x;    // input rows [kMaxRows][K]
+    const int16_t *norm; // RMSNorm weights [K] (nullptr: no norm prologue)
+    int32_t inv_elems;   // recip(fm(K)) in Q8.8
+    int32_t inv_rms_const; // inv_rms when inv_elems == 0 (input-independent)
+    const Step *step;
+    int16_t *out;        // EPI_QKV: q [8][Hq]; EPI_RESID: hidden [8][Ho]; EPI_SILU: act [8][I]
+    int out_stride;
+    const int16_t *resid; // EPI_RESID residual rows [8][out_stride]
+    int64_t *partial;    // EPI_PARTIAL [8][2*npairs]
+    const int16_t *etab; // SiLU exp table (2049 entries, index raw+2048)
+    // EPI_QKV
+    int16_t *kc;         // K cache of this layer [kv_heads][max_seq][hd]
+    int16_t *vc;
+    const int16_t *rope; // [max_seq][hd]: cos half | sin half, Q8.8
+    int hd;
+    int q_pairs;         // pairs belonging to Q (local heads * hd/2)
+    int kv_pairs;        // pairs of K (= of V) (kv_heads * hd/2)
+    int max_seq;
+};
+
+struct AttnArgs {
+    const int16_t *q;    // [8][q_heads*hd] post-RoPE queries of this rank
+    const int16_t *kc;   // layer K cache [kv_heads][max_seq][hd]
+    const int16_t *vc;
+    int16_t *scores;     // [8][q_heads][max_seq]
+    int16_t *tmax;       // [8][q_heads][max_tiles]
+    int16_t *tval;       // [8][q_heads][max_tiles][hd]
+    int32_t *tsum;       // [8][q_heads][max_tiles]
+    int16_t *told;       // [8][q_heads][max_tiles]
+    uint32_t *tickets;   // [8][kv_groups]
+    int16_t *out;        // [8][q_heads*hd]
+    const int16_t *ptab; // softmax exp table (2049 entries)
+    const Step *step;
+    int q_heads;         // query heads on this rank
+    int group;           // query heads per KV head
+    int kv_first;        // first KV head used by this rank
+    int hd;
+    int max_seq;
+    int max_tiles;
+    int32_t qk_scale;    // accum(fm(1/sqrt(hd))) raw, Q16.16
+};
+
+struct NormArgs {
+    const int16_t *x;
+    const int16_t *w;
+    int16_t *y;
+    int n;
+    int32_t inv_elems;
+    int32_t inv_rms_const;
+    const Step *step;
+};
+
+struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduce)
+    const int64_t *partial;
+    const int16_t *resid;
+    int16_t *out;
+    int n;
+    const Step *step;
+};
+
+// Launchers (stream-ordered, programmatic-dependent launch enabled).
+cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
+cudaError_t launch_attn_scores(const AttnArgs &a, int rows, cudaStream_t s);
+cudaError_t launch_attn_pv(const AttnArgs &a, int rows, cudaStream_t s);
+cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
+cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
+size_t proj_smem_bytes(int rows_tmpl, int K);
+cudaError_t proj_configure(int max_smem_bytes);
+int proj_max_ctas_per_sm(int epi, int rows_tmpl, int K);
+
+// Weight layout kernel (model upload): slot s of the destination receives
+// dense row row_of_slot[s], columns [col0, col0+K), as K/2 32-bit words; word j
+// holds bytes {lo(w[2j]), lo(w[2j+1]), hi(w[2j]), hi(w[2j+1])} so that one dp2a.lo
+// (unsigned low bytes) plus one dp2a.hi (signed high bytes) form two exact
+// int16 x int16 products against a packed pair of activations.
+cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
+                              const int32_t *row_of_slot, int nslots, uint32_t *dst,
+                              cudaStream_t s);
+
+}  // namespace llmx

@@ -1,0 +1,635 @@
+// Device context of the resident decoder-layer path: accelerator_t
+// (host/host_qwen_8x64.cpp:1024-3087) rebuilt around one CUDA stream, HBM-
+// resident weights / KV cache / hidden ping-pong buffers, and one CUDA graph per
+// decoder stack (2L+1 coarse tasks) instead of per-task XRT enqueues.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "fixed.cuh"
+#include "host_model.h"
+#include "kernels.cuh"
+
+using namespace llmx;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail_cuda(cudaError_t e, const char *what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return LLMX_ERR_CUDA;
+}
+
+#define CK(call)                                          \
+    do {                                                  \
+        cudaError_t e_ = (call);                          \
+        if (e_ != cudaSuccess) return fail_cuda(e_, #call); \
+    } while (0)
+
+#define CKN(call)                                                             \
+    do {                                                                      \
+        ncclResult_t r_ = (call);                                             \
+        if (r_ != ncclSuccess) {                                              \
+            g_last_error = std::string(#call) + ": " + ncclGetErrorString(r_); \
+            return LLMX_ERR_NCCL;                                             \
+        }                                                                     \
+    } while (0)
+
+__global__ void k_set_step(Step *dst, int32_t position, int32_t rows) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    dst->position = position;
+    dst->rows = rows;
+}
+
+int rows_template(uint32_t rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8; }
+
+}  // namespace
+
+struct llmx_ctx {
+    llmx_shape s{};
+    int dev = 0, rank = 0, size = 1, nsm = 148;
+    ncclComm_t comm = nullptr;
+    cudaStream_t stream = nullptr;
+    // geometry of this rank
+    int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, max_tiles = 0;
+    // weights: per layer [QKV | O | GU | D] words
+    size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
+    uint32_t *wbuf = nullptr;
+    int16_t *staging = nullptr;
+    int32_t *slot_qkv = nullptr, *slot_o = nullptr, *slot_gu = nullptr, *slot_d = nullptr;
+    int16_t *norms = nullptr, *rope = nullptr, *etab = nullptr, *ptab = nullptr;
+    int16_t *kc = nullptr, *vc = nullptr;
+    int16_t *hid[2] = {nullptr, nullptr};
+    int16_t *q = nullptr, *att = nullptr, *act = nullptr;
+    int64_t *partial = nullptr;
+    int16_t *scores = nullptr, *tmax = nullptr, *tval = nullptr, *told = nullptr;
+    int32_t *tsum = nullptr;
+    uint32_t *tickets = nullptr;
+    Step *step = nullptr;
+    int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
+    uint32_t out_pair = 0, in_pair = 1;
+    std::vector<bool> layer_loaded;
+    bool norms_loaded = false;
+    uint64_t launches = 0, last_launches = 0, device_bytes = 0;
+    std::map<std::tuple<uint32_t, uint32_t, uint32_t, int>, std::pair<cudaGraphExec_t, uint64_t>> graphs;
+    std::vector<void *> allocations;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(llmx_ctx *c, T **p, size_t count) {
+    void *v = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess) {
+        g_last_error = std::string("cudaMalloc: ") + cudaGetErrorString(e);
+        return LLMX_ERR_NOMEM;
+    }
+    CK(cudaMemset(v, 0, bytes));
+    c->allocations.push_back(v);
+    c->device_bytes += bytes;
+    *p = static_cast<T *>(v);
+    return LLMX_OK;
+}
+
+int16_t *kc_layer(const llmx_ctx *c, uint32_t layer) {
+    return c->kc + (size_t)layer * c->s.kv_heads * c->s.max_seq * c->hd;
+}
+int16_t *vc_layer(const llmx_ctx *c, uint32_t layer) {
+    return c->vc + (size_t)layer * c->s.kv_heads * c->s.max_seq * c->hd;
+}
+const uint32_t *wl(const llmx_ctx *c, uint32_t layer) { return c->wbuf + (size_t)layer * c->layer_words; }
+
+int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
+    const int want = (npairs + kWarps - 1) / kWarps;
+    int occ = proj_max_ctas_per_sm(0, rt, K);
+    if (occ < 1) occ = 1;
+    return std::max(1, std::min(want, c->nsm * occ));
+}
+
+int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
+    CKN(ncclAllReduce(c->partial, c->partial, (size_t)rows * c->s.hidden, ncclInt64, ncclSum, c->comm,
+                      c->stream));
+    ResidArgs r{c->partial, resid, out, c->s.hidden, c->step};
+    CK(launch_round_resid(r, (int)rows, c->stream));
+    c->launches += 1;
+    return LLMX_OK;
+}
+
+// Enqueue the kernels of one coarse task on the context stream.
+int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32_t in_pair,
+                 uint32_t out_pair) {
+    const llmx_shape &s = c->s;
+    const int rt = rows_template(rows);
+    const int16_t *in = c->hid[in_pair];
+    int16_t *out = c->hid[out_pair];
+    if (op == LLMX_OP_ATTENTION_SUBLAYER) {
+        ProjArgs a{};
+        a.w = wl(c, layer);
+        a.K = s.hidden;
+        a.npairs = (c->Hq + 2 * c->KV) / 2;
+        a.x = in;
+        a.norm = c->norms + (size_t)2 * layer * s.hidden;
+        a.inv_elems = c->inv_elems;
+        a.inv_rms_const = c->inv_rms_const;
+        a.step = c->step;
+        a.out = c->q;
+        a.out_stride = c->Hq;
+        a.kc = kc_layer(c, layer);
+        a.vc = vc_layer(c, layer);
+        a.rope = c->rope;
+        a.hd = c->hd;
+        a.q_pairs = c->Hq / 2;
+        a.kv_pairs = c->KV / 2;
+        a.max_seq = s.max_seq;
+        CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
+        AttnArgs t{};
+        t.q = c->q;
+        t.kc = kc_layer(c, layer);
+        t.vc = vc_layer(c, layer);
+        t.scores = c->scores;
+        t.tmax = c->tmax;
+        t.tval = c->tval;
+        t.tsum = c->tsum;
+        t.told = c->told;
+        t.tickets = c->tickets;
+        t.out = c->att;
+        t.ptab = c->ptab;
+        t.step = c->step;
+        t.q_heads = c->hq;
+        t.group = std::min(c->G, c->hq);
+        t.kv_first = c->h0 / c->G;
+        t.hd = c->hd;
+        t.max_seq = s.max_seq;
+        t.max_tiles = c->max_tiles;
+        t.qk_scale = c->qk_scale;
+        CK(launch_attn_scores(t, (int)rows, c->stream));
+        CK(launch_attn_pv(t, (int)rows, c->stream));
+        ProjArgs o{};
+        o.w = wl(c, layer) + c->w_qkv;
+        o.K = c->Hq;
+        o.npairs = s.hidden / 2;
+        o.x = c->att;
+        o.step = c->step;
+        o.out = out;
+        o.out_stride = s.hidden;
+        o.resid = in;
+        o.partial = c->partial;
+        const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+        CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
+        c->launches += 4;
+        if (c->size > 1) return allreduce_resid(c, rows, out, in);
+        return LLMX_OK;
+    }
+    if (op == LLMX_OP_FFN_SUBLAYER) {
+        ProjArgs g{};
+        g.w = wl(c, layer) + c->w_qkv + c->w_o;
+        g.K = s.hidden;
+        g.npairs = c->Il;
+        g.x = in;
+        g.norm = c->norms + (size_t)(2 * layer + 1) * s.hidden;
+        g.inv_elems = c->inv_elems;
+        g.inv_rms_const = c->inv_rms_const;
+        g.step = c->step;
+        g.out = c->act;
+        g.out_stride = c->Il;
+        g.etab = c->etab;
+        CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
+        ProjArgs d{};
+        d.w = wl(c, layer) + c->w_qkv + c->w_o + c->w_gu;
+        d.K = c->Il;
+        d.npairs = s.hidden / 2;
+        d.x = c->act;
+        d.step = c->step;
+        d.out = out;
+        d.out_stride = s.hidden;
+        d.resid = in;
+        d.partial = c->partial;
+        const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+        CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
+        c->launches += 2;
+        if (c->size > 1) return allreduce_resid(c, rows, out, in);
+        return LLMX_OK;
+    }
+    if (op == LLMX_OP_FINAL_NORM) {
+        NormArgs n{in, c->norms + (size_t)2 * s.layers * s.hidden, out, s.hidden, c->inv_elems,
+                   c->inv_rms_const, c->step};
+        CK(launch_rmsnorm(n, (int)rows, c->stream));
+        c->launches += 1;
+        return LLMX_OK;
+    }
+    return LLMX_OK;  // NOP
+}
+
+int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
+    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows);
+    CK(cudaGetLastError());
+    c->launches += 1;
+    return LLMX_OK;
+}
+
+bool model_ready(const llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count) {
+    if (!c->norms_loaded) return false;
+    for (uint32_t l = layer_begin; l < layer_begin + layer_count; l++)
+        if (!c->layer_loaded[l]) return false;
+    return true;
+}
+
+// Kernels of a stack, enqueued (graph capture body).
+int enqueue_stack(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, int final_norm) {
+    for (uint32_t l = layer_begin; l < layer_begin + layer_count; l++) {
+        int rc = enqueue_task(c, LLMX_OP_ATTENTION_SUBLAYER, l, rows, 1, 0);
+        if (rc) return rc;
+        rc = enqueue_task(c, LLMX_OP_FFN_SUBLAYER, l, rows, 0, 1);
+        if (rc) return rc;
+    }
+    if (final_norm) return enqueue_task(c, LLMX_OP_FINAL_NORM, 0, rows, 1, 0);
+    return LLMX_OK;
+}
+
+int launch_stack_graph(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, int final_norm) {
+    const auto key = std::make_tuple(rows, layer_begin, layer_count, final_norm);
+    auto it = c->graphs.find(key);
+    if (it == c->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        const uint64_t before = c->launches;
+        const int rc = enqueue_stack(c, rows, layer_begin, layer_count, final_norm);
+        cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return fail_cuda(e, "cudaStreamEndCapture");
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return fail_cuda(e, "cudaGraphInstantiate");
+        it = c->graphs.emplace(key, std::make_pair(exec, c->launches - before)).first;
+        c->launches = before;
+    }
+    CK(cudaGraphLaunch(it->second.first, c->stream));
+    c->launches += it->second.second;
+    return LLMX_OK;
+}
+
+void release(llmx_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->dev);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.first);
+    c->graphs.clear();
+    if (c->comm) ncclCommDestroy(c->comm);
+    for (void *p : c->allocations) cudaFree(p);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *llmx_last_error(void) { return g_last_error.c_str(); }
+
+int llmx_tp_unique_id(void *id128) {
+    if (!id128) return LLMX_ERR_ARG;
+    ncclUniqueId id;
+    CKN(ncclGetUniqueId(&id));
+    std::memcpy(id128, &id, sizeof(id));
+    return LLMX_OK;
+}
+
+int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, const void *tp_id,
+                llmx_ctx **out) {
+    if (!shape || !out) return LLMX_ERR_ARG;
+    *out = nullptr;
+    int rc = llmx_shape_validate(shape);
+    if (rc) return rc;
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !tp_id)) return LLMX_ERR_ARG;
+    const llmx_shape &s = *shape;
+    // tensor parallel split: Q/O heads and FFN columns; 8-feature granularity
+    if (s.heads % tp_size || s.inter % (8 * tp_size)) return LLMX_ERR_UNSUPPORTED;
+    const int hd = s.hidden / s.heads, G = s.heads / s.kv_heads, hq = s.heads / tp_size;
+    if (!(hq % G == 0 || G % hq == 0) || (hq * hd) % 8) return LLMX_ERR_UNSUPPORTED;
+    llmx_ctx *c = new llmx_ctx();
+    c->s = s;
+    c->dev = device;
+    c->rank = tp_rank;
+    c->size = tp_size;
+    c->hd = hd;
+    c->G = G;
+    c->KV = s.kv_heads * hd;
+    c->hq = hq;
+    c->h0 = tp_rank * hq;
+    c->Hq = hq * hd;
+    c->Il = s.inter / tp_size;
+    c->c0 = tp_rank * c->Il;
+    c->max_tiles = (s.max_seq + kTile - 1) / kTile;
+    c->layer_loaded.assign(s.layers, false);
+    auto bail = [&](int code) {
+        release(c);
+        return code;
+    };
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return bail(fail_cuda(e, "cudaSetDevice"));
+    cudaDeviceProp prop{};
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return bail(fail_cuda(e, "cudaGetDeviceProperties"));
+    c->nsm = prop.multiProcessorCount;
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
+    e = proj_configure(200 * 1024);
+    if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
+
+    const size_t H = s.hidden;
+    c->w_qkv = (size_t)(c->Hq + 2 * c->KV) * H / 2;
+    c->w_o = H * (size_t)c->Hq / 2;
+    c->w_gu = (size_t)2 * c->Il * H / 2;
+    c->w_d = H * (size_t)c->Il / 2;
+    c->layer_words = c->w_qkv + c->w_o + c->w_gu + c->w_d;
+    const size_t kv_elems = (size_t)s.layers * s.kv_heads * s.max_seq * hd;
+    const size_t mt = c->max_tiles;
+    if ((rc = dalloc(c, &c->wbuf, c->layer_words * s.layers)) ||
+        (rc = dalloc(c, &c->staging, layer_elems(s))) ||
+        (rc = dalloc(c, &c->slot_qkv, c->Hq + 2 * c->KV)) || (rc = dalloc(c, &c->slot_o, H)) ||
+        (rc = dalloc(c, &c->slot_gu, 2 * c->Il)) || (rc = dalloc(c, &c->slot_d, H)) ||
+        (rc = dalloc(c, &c->norms, (2 * (size_t)s.layers + 1) * H)) ||
+        (rc = dalloc(c, &c->rope, (size_t)s.max_seq * hd)) || (rc = dalloc(c, &c->etab, 2049)) ||
+        (rc = dalloc(c, &c->ptab, 2049)) || (rc = dalloc(c, &c->kc, kv_elems)) ||
+        (rc = dalloc(c, &c->vc, kv_elems)) || (rc = dalloc(c, &c->hid[0], kMaxRows * H)) ||
+        (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
+        (rc = dalloc(c, &c->att, kMaxRows * (size_t)c->Hq)) ||
+        (rc = dalloc(c, &c->act, kMaxRows * (size_t)c->Il)) || (rc = dalloc(c, &c->partial, kMaxRows * H)) ||
+        (rc = dalloc(c, &c->scores, kMaxRows * (size_t)hq * s.max_seq)) ||
+        (rc = dalloc(c, &c->tmax, kMaxRows * (size_t)hq * mt)) ||
+        (rc = dalloc(c, &c->tval, kMaxRows * (size_t)hq * mt * hd)) ||
+        (rc = dalloc(c, &c->tsum, kMaxRows * (size_t)hq * mt)) ||
+        (rc = dalloc(c, &c->told, kMaxRows * (size_t)hq * mt)) ||
+        (rc = dalloc(c, &c->tickets, kMaxRows * (size_t)s.kv_heads)) || (rc = dalloc(c, &c->step, 1)))
+        return bail(rc);
+
+    // slot -> dense row tables of the pair-interleaved layout
+    {
+        std::vector<int32_t> t;
+        const int half = hd / 2;
+        for (int lh = 0; lh < hq; lh++)  // Q rows of this rank's heads: pairs (i, i+hd/2)
+            for (int i = 0; i < half; i++) {
+                t.push_back((c->h0 + lh) * hd + i);
+                t.push_back((c->h0 + lh) * hd + half + i);
+            }
+        for (int seg = 1; seg <= 2; seg++)  // K then V rows (dense rows after Q)
+            for (int kh = 0; kh < s.kv_heads; kh++)
+                for (int i = 0; i < half; i++) {
+                    t.push_back((int)H + (seg - 1) * c->KV + kh * hd + i);
+                    t.push_back((int)H + (seg - 1) * c->KV + kh * hd + half + i);
+                }
+        e = cudaMemcpy(c->slot_qkv, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "slot upload"));
+        t.clear();
+        for (int r = 0; r < (int)H; r++) t.push_back(r);
+        e = cudaMemcpy(c->slot_o, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->slot_d, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "slot upload"));
+        t.clear();
+        for (int p = 0; p < c->Il; p++) {  // gate row, up row (up rows follow the gate rows)
+            t.push_back(c->c0 + p);
+            t.push_back(s.inter + c->c0 + p);
+        }
+        e = cudaMemcpy(c->slot_gu, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "slot upload"));
+    }
+    // constant tables
+    {
+        std::vector<int16_t> e16(2049), p18(2049), rope((size_t)s.max_seq * hd);
+        build_exp_tables(e16.data(), p18.data());
+        build_rope_table(hd, s.max_seq, rope.data());
+        e = cudaMemcpy(c->etab, e16.data(), 2049 * 2, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->ptab, p18.data(), 2049 * 2, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(c->rope, rope.data(), rope.size() * 2, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "table upload"));
+        c->inv_elems = recip_q88(fm_from_count(s.hidden));
+        c->inv_rms_const = inv_rms_q88(0, 0);
+        c->qk_scale = qk_scale_q1616(hd);
+    }
+    if (tp_size > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, tp_id, sizeof(id));
+        ncclResult_t r = ncclCommInitRank(&c->comm, tp_size, id, tp_rank);
+        if (r != ncclSuccess) {
+            g_last_error = std::string("ncclCommInitRank: ") + ncclGetErrorString(r);
+            return bail(LLMX_ERR_NCCL);
+        }
+    }
+    *out = c;
+    return LLMX_OK;
+}
+
+int llmx_destroy(llmx_ctx *c) {
+    release(c);
+    return LLMX_OK;
+}
+
+int llmx_upload_layer(llmx_ctx *c, uint32_t layer, const int16_t *dense) {
+    if (!c || !dense || layer >= (uint32_t)c->s.layers) return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s;
+    CK(cudaSetDevice(c->dev));
+    size_t off[8];
+    layer_offsets(s, off);
+    CK(cudaMemcpyAsync(c->staging, dense, layer_elems(s) * 2, cudaMemcpyHostToDevice, c->stream));
+    uint32_t *w = c->wbuf + (size_t)layer * c->layer_words;
+    const int H = s.hidden;
+    // Q,K,V are consecutive dense matrices with row length H
+    CK(launch_pack_pairs(c->staging + off[0], H, 0, H, c->slot_qkv, c->Hq + 2 * c->KV, w, c->stream));
+    CK(launch_pack_pairs(c->staging + off[3], H, c->h0 * c->hd, c->Hq, c->slot_o, H, w + c->w_qkv, c->stream));
+    CK(launch_pack_pairs(c->staging + off[4], H, 0, H, c->slot_gu, 2 * c->Il, w + c->w_qkv + c->w_o, c->stream));
+    CK(launch_pack_pairs(c->staging + off[6], s.inter, c->c0, c->Il, c->slot_d, H,
+                         w + c->w_qkv + c->w_o + c->w_gu, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->layer_loaded[layer] = true;
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.first);
+    c->graphs.clear();
+    return LLMX_OK;
+}
+
+int llmx_upload_norms(llmx_ctx *c, const int16_t *norms) {
+    if (!c || !norms) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    CK(cudaMemcpy(c->norms, norms, (2 * (size_t)c->s.layers + 1) * c->s.hidden * 2, cudaMemcpyHostToDevice));
+    c->norms_loaded = true;
+    return LLMX_OK;
+}
+
+int llmx_upload_model(llmx_ctx *c, const llmx_model *m) {
+    if (!c || !m) return LLMX_ERR_ARG;
+    if (std::memcmp(&c->s, &m->shape, sizeof(llmx_shape)) != 0) return LLMX_ERR_ARG;
+    if (m->norms.empty()) return LLMX_ERR_STATE;
+    int rc = llmx_upload_norms(c, m->norms.data());
+    if (rc) return rc;
+    for (size_t l = 0; l < m->layers.size(); l++)
+        if (!m->layers[l].empty() && (rc = llmx_upload_layer(c, (uint32_t)l, m->layers[l].data()))) return rc;
+    return LLMX_OK;
+}
+
+int llmx_reset_kv(llmx_ctx *c) {
+    if (!c) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    const size_t n = (size_t)c->s.layers * c->s.kv_heads * c->s.max_seq * c->hd * 2;
+    CK(cudaMemsetAsync(c->kc, 0, n, c->stream));
+    CK(cudaMemsetAsync(c->vc, 0, n, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+static int kv_copy(llmx_ctx *c, uint32_t layer, uint32_t position, uint32_t count, int16_t *k, int16_t *v,
+                   bool to_device) {
+    if (!c || !k || !v || layer >= (uint32_t)c->s.layers || (uint64_t)position + count > (uint64_t)c->s.max_seq)
+        return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    const size_t row = (size_t)c->hd * 2, n = (size_t)count * row;
+    for (int h = 0; h < c->s.kv_heads; h++) {
+        int16_t *dk = kc_layer(c, layer) + ((size_t)h * c->s.max_seq + position) * c->hd;
+        int16_t *dv = vc_layer(c, layer) + ((size_t)h * c->s.max_seq + position) * c->hd;
+        int16_t *hk = k + (size_t)h * count * c->hd, *hv = v + (size_t)h * count * c->hd;
+        if (to_device) {
+            CK(cudaMemcpyAsync(dk, hk, n, cudaMemcpyHostToDevice, c->stream));
+            CK(cudaMemcpyAsync(dv, hv, n, cudaMemcpyHostToDevice, c->stream));
+        } else {
+            CK(cudaMemcpyAsync(hk, dk, n, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaMemcpyAsync(hv, dv, n, cudaMemcpyDeviceToHost, c->stream));
+        }
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+int llmx_write_kv(llmx_ctx *c, uint32_t layer, uint32_t position, uint32_t count, const int16_t *k,
+                  const int16_t *v) {
+    return kv_copy(c, layer, position, count, const_cast<int16_t *>(k), const_cast<int16_t *>(v), true);
+}
+
+int llmx_read_kv(llmx_ctx *c, uint32_t layer, uint32_t position, uint32_t count, int16_t *k, int16_t *v) {
+    return kv_copy(c, layer, position, count, k, v, false);
+}
+
+int llmx_write_hidden(llmx_ctx *c, uint32_t pair, const int16_t *rows_host, uint32_t rows) {
+    if (!c || pair > 1 || !rows_host || rows > LLMX_MAX_ROWS) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    CK(cudaMemcpyAsync(c->hid[pair], rows_host, (size_t)rows * c->s.hidden * 2, cudaMemcpyHostToDevice,
+                       c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+int llmx_read_hidden(llmx_ctx *c, uint32_t pair, int16_t *rows_host, uint32_t rows) {
+    if (!c || pair > 1 || !rows_host || rows > LLMX_MAX_ROWS) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    CK(cudaMemcpyAsync(rows_host, c->hid[pair], (size_t)rows * c->s.hidden * 2, cudaMemcpyDeviceToHost,
+                       c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+int llmx_bind(llmx_ctx *c, uint32_t out_pair, uint32_t in_pair) {
+    if (!c || out_pair > 1 || in_pair > 1 || out_pair == in_pair) return LLMX_ERR_ARG;
+    c->out_pair = out_pair;
+    c->in_pair = in_pair;
+    return LLMX_OK;
+}
+
+int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint32_t rows, llmx_status *st) {
+    llmx_status local;
+    if (!st) st = &local;
+    if (!c) return LLMX_ERR_ARG;
+    const int code = llmx_validate_task(&c->s, op, layer, position, rows, st);
+    if (code != LLMX_OK || op == LLMX_OP_NOP) return code;
+    if (op != LLMX_OP_FINAL_NORM && !model_ready(c, layer, 1)) return LLMX_ERR_STATE;
+    if (op == LLMX_OP_FINAL_NORM && !c->norms_loaded) return LLMX_ERR_STATE;
+    CK(cudaSetDevice(c->dev));
+    const uint64_t before = c->launches;
+    int rc = set_step(c, position, rows);
+    if (!rc) rc = enqueue_task(c, op, layer, rows, c->in_pair, c->out_pair);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(c->stream));
+    c->last_launches = c->launches - before;
+    return LLMX_OK;
+}
+
+int llmx_stack_async(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, uint32_t position,
+                     int include_final_norm) {
+    if (!c) return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s;
+    if (rows == 0 || rows > LLMX_MAX_ROWS || layer_count == 0 || layer_begin >= (uint32_t)s.layers ||
+        layer_begin + layer_count > (uint32_t)s.layers || position >= (uint32_t)s.max_seq ||
+        position + rows > (uint32_t)s.max_seq)
+        return LLMX_ERR_ARG;  // run_composed_decoder_stack host:1266-1281
+    if (!model_ready(c, layer_begin, layer_count)) return LLMX_ERR_STATE;
+    CK(cudaSetDevice(c->dev));
+    const uint64_t before = c->launches;
+    int rc = set_step(c, position, rows);
+    if (!rc) rc = launch_stack_graph(c, rows, layer_begin, layer_count, include_final_norm ? 1 : 0);
+    c->last_launches = c->launches - before;
+    return rc;
+}
+
+int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t layer_begin, uint32_t layer_count,
+               uint32_t position, int include_final_norm, int materialize, int16_t *hidden_out,
+               llmx_status *last) {
+    if (!c || !hidden_in || (materialize && !hidden_out)) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    if (rows == 0 || rows > LLMX_MAX_ROWS) return LLMX_ERR_ARG;
+    CK(cudaMemcpyAsync(c->hid[1], hidden_in, (size_t)rows * c->s.hidden * 2, cudaMemcpyHostToDevice, c->stream));
+    int rc = llmx_stack_async(c, rows, layer_begin, layer_count, position, include_final_norm);
+    if (rc) return rc;
+    if (materialize)
+        CK(cudaMemcpyAsync(hidden_out, c->hid[include_final_norm ? 0 : 1], (size_t)rows * c->s.hidden * 2,
+                           cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (last) {
+        const uint32_t op = include_final_norm ? LLMX_OP_FINAL_NORM : LLMX_OP_FFN_SUBLAYER;
+        llmx_validate_task(&c->s, op, include_final_norm ? 0 : layer_begin + layer_count - 1, position, rows,
+                           last);
+    }
+    return LLMX_OK;
+}
+
+int llmx_synchronize(llmx_ctx *c) {
+    if (!c) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+void *llmx_stream(llmx_ctx *c) { return c ? (void *)c->stream : nullptr; }
+void *llmx_hidden_device_ptr(llmx_ctx *c, uint32_t pair) { return c && pair < 2 ? c->hid[pair] : nullptr; }
+uint64_t llmx_kernel_launches(const llmx_ctx *c) { return c ? c->last_launches : 0; }
+uint64_t llmx_device_bytes(const llmx_ctx *c) { return c ? c->device_bytes : 0; }
+
+int llmx_run_prompt_block(llmx_ctx *c, const llmx_model *m, const uint32_t *tokens, uint32_t n, uint32_t position,
+                          int materialize, int16_t *hidden_out) {
+    if (!c || !m || !tokens || n == 0 || n > LLMX_MAX_ROWS) return LLMX_ERR_ARG;
+    std::vector<int16_t> rows((size_t)n * c->s.hidden);
+    int rc = llmx_model_embed(m, tokens, n, rows.data());
+    if (rc) return rc;
+    return llmx_stack(c, rows.data(), n, 0, (uint32_t)c->s.layers, position, materialize, materialize,
+                      hidden_out, nullptr);
+}
+
+int llmx_run_token(llmx_ctx *c, const llmx_model *m, uint32_t token, uint32_t position, int16_t *hidden_out) {
+    if (!c || !m || !hidden_out) return LLMX_ERR_ARG;
+    std::vector<int16_t> row(c->s.hidden);
+    int rc = llmx_model_embed(m, &token, 1, row.data());
+    if (rc) return rc;
+    return llmx_stack(c, row.data(), 1, 0, (uint32_t)c->s.layers, position, 1, 1, hidden_out, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,363 @@
+"""Python mirror of the llmx C ABI (include/llmx.h) over ctypes.
+
+Mirrors the reference host interfaces of host/host_qwen_8x64.cpp in the
+LLM-ACCEL tree: ``Accelerator`` ~ accelerator_t (run_composed_decoder_stack,
+execute_bound_resident_task, bind_controller_data_ports), ``Model`` ~
+model_data_t, ``Executor`` ~ qwen_executor_t.  Errors raise ``LlmxError``
+carrying the controller status code, as the reference host throws on a bad
+status (check_status host:3028-3049).
+
+The compute path is the CUDA library libllmx.so built from csrc/; importing
+this module never falls back to a CPU implementation -- a missing library or
+GPU is an error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libllmx.so")
+
+OK = 0
+BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 3, 4, 5
+ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED = range(100, 108)
+OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
+MAX_ROWS = 8
+
+
+class LlmxError(RuntimeError):
+    def __init__(self, code, what=""):
+        self.code = code
+        msg = f"{what}: {strerror(code)} ({code})"
+        detail = last_error()
+        if detail:
+            msg += f" [{detail}]"
+        super().__init__(msg)
+
+
+class Shape(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in
+                ("vocab", "hidden", "inter", "layers", "heads", "kv_heads", "max_seq")]
+
+    @property
+    def head_dim(self):
+        return self.hidden // self.heads
+
+    @property
+    def kv_channels(self):
+        return self.kv_heads * self.head_dim
+
+    def tuple(self):
+        return tuple(getattr(self, f) for f, _ in self._fields_)
+
+
+class Status(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("op", "code", "token_count", "output_waves", "mm_tasks",
+                                          "vector_tasks", "completed_packets", "last_task")] + \
+               [("reserved", C.c_uint32 * 8)]
+
+    def as_dict(self):
+        return {f: getattr(self, f) for f, _ in self._fields_ if f != "reserved"}
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python llm-accel_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        i16p = np.ctypeslib.ndpointer(np.int16, flags="C_CONTIGUOUS")
+        u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+        vp, sp, stp = C.c_void_p, C.POINTER(Shape), C.POINTER(Status)
+        sig = {
+            "llmx_profile": (C.c_int, [C.c_char_p, sp]),
+            "llmx_shape_validate": (C.c_int, [sp]),
+            "llmx_validate_task": (C.c_int, [sp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, stp]),
+            "llmx_strerror": (C.c_char_p, [C.c_int]),
+            "llmx_last_error": (C.c_char_p, []),
+            "llmx_exp_tables": (C.c_int, [i16p, i16p]),
+            "llmx_rope_table": (C.c_int, [C.c_int, C.c_int, i16p]),
+            "llmx_gauss_fill": (C.c_int, [C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, i16p, C.c_size_t]),
+            "llmx_model_create": (C.c_int, [sp, C.POINTER(vp)]),
+            "llmx_model_destroy": (None, [vp]),
+            "llmx_model_init_reference_random": (C.c_int, [vp, C.c_uint32, C.c_int]),
+            "llmx_model_init_gaussian": (C.c_int, [vp, C.c_uint64, C.c_double, C.c_int]),
+            "llmx_model_load_packed": (C.c_int, [vp, C.c_char_p, C.c_int]),
+            "llmx_layer_weight_elems": (C.c_size_t, [sp]),
+            "llmx_model_layer": (C.POINTER(C.c_int16), [vp, C.c_uint32]),
+            "llmx_model_norms": (C.POINTER(C.c_int16), [vp]),
+            "llmx_model_embedding": (C.POINTER(C.c_int16), [vp]),
+            "llmx_model_embed": (C.c_int, [vp, u32p, C.c_uint32, i16p]),
+            "llmx_model_lm_head_argmax": (C.c_int, [vp, i16p, C.c_int, C.POINTER(C.c_uint32)]),
+            "llmx_tp_unique_id": (C.c_int, [vp]),
+            "llmx_create": (C.c_int, [sp, C.c_int, C.c_int, C.c_int, vp, C.POINTER(vp)]),
+            "llmx_destroy": (C.c_int, [vp]),
+            "llmx_upload_model": (C.c_int, [vp, vp]),
+            "llmx_upload_layer": (C.c_int, [vp, C.c_uint32, i16p]),
+            "llmx_upload_norms": (C.c_int, [vp, i16p]),
+            "llmx_reset_kv": (C.c_int, [vp]),
+            "llmx_write_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i16p, i16p]),
+            "llmx_read_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i16p, i16p]),
+            "llmx_write_hidden": (C.c_int, [vp, C.c_uint32, i16p, C.c_uint32]),
+            "llmx_read_hidden": (C.c_int, [vp, C.c_uint32, i16p, C.c_uint32]),
+            "llmx_bind": (C.c_int, [vp, C.c_uint32, C.c_uint32]),
+            "llmx_task": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, stp]),
+            "llmx_stack": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int,
+                                     C.c_int, vp, stp]),
+            "llmx_stack_async": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int]),
+            "llmx_synchronize": (C.c_int, [vp]),
+            "llmx_stream": (vp, [vp]),
+            "llmx_hidden_device_ptr": (vp, [vp, C.c_uint32]),
+            "llmx_kernel_launches": (C.c_uint64, [vp]),
+            "llmx_device_bytes": (C.c_uint64, [vp]),
+            "llmx_run_prompt_block": (C.c_int, [vp, vp, u32p, C.c_uint32, C.c_uint32, C.c_int, i16p]),
+            "llmx_run_token": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, i16p]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def strerror(code):
+    return lib().llmx_strerror(code).decode()
+
+
+def last_error():
+    return lib().llmx_last_error().decode()
+
+
+def check(rc, what=""):
+    if rc != OK:
+        raise LlmxError(rc, what)
+
+
+def profile(name) -> Shape:
+    s = Shape()
+    check(lib().llmx_profile(name.encode(), C.byref(s)), f"profile {name}")
+    return s
+
+
+def shape(name_or_tuple, **overrides) -> Shape:
+    s = profile(name_or_tuple) if isinstance(name_or_tuple, str) else Shape(*name_or_tuple)
+    for k, v in overrides.items():
+        setattr(s, k, v)
+    return s
+
+
+def validate_task(s: Shape, op, layer, position, rows):
+    st = Status()
+    code = lib().llmx_validate_task(C.byref(s), op, layer, position, rows, C.byref(st))
+    return code, st
+
+
+def exp_tables():
+    e = np.zeros(2049, np.int16)
+    p = np.zeros(2049, np.int16)
+    check(lib().llmx_exp_tables(e, p))
+    return e, p
+
+
+def rope_table(head_dim, max_seq):
+    t = np.zeros((max_seq, head_dim), np.int16)
+    check(lib().llmx_rope_table(head_dim, max_seq, t))
+    return t
+
+
+def gauss_fill(seed, stream, sigma_raw, n, index0=0):
+    out = np.zeros(n, np.int16)
+    check(lib().llmx_gauss_fill(seed, stream, sigma_raw, index0, out, n))
+    return out
+
+
+class Model:
+    """model_data_t host:779-1022: dense per-layer weights, norms, embedding, LM head."""
+
+    def __init__(self, s: Shape):
+        self.shape = s
+        self.h = C.c_void_p()
+        check(lib().llmx_model_create(C.byref(s), C.byref(self.h)), "model_create")
+
+    def close(self):
+        if self.h:
+            lib().llmx_model_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_reference_random(self, seed, keep_layers=0):
+        check(lib().llmx_model_init_reference_random(self.h, seed, keep_layers), "init_reference_random")
+        return self
+
+    def init_gaussian(self, seed, w_sigma=0.02, lm_head=False):
+        check(lib().llmx_model_init_gaussian(self.h, seed, w_sigma, int(lm_head)), "init_gaussian")
+        return self
+
+    def load_packed(self, directory, tie_embeddings=False):
+        check(lib().llmx_model_load_packed(self.h, directory.encode(), int(tie_embeddings)), "load_packed")
+        return self
+
+    def layer(self, l) -> np.ndarray:
+        n = lib().llmx_layer_weight_elems(C.byref(self.shape))
+        p = lib().llmx_model_layer(self.h, l)
+        if not p:
+            raise LlmxError(ERR_STATE, f"layer {l} not resident")
+        return np.ctypeslib.as_array(p, shape=(n,))
+
+    def norms(self) -> np.ndarray:
+        s = self.shape
+        return np.ctypeslib.as_array(lib().llmx_model_norms(self.h), shape=(2 * s.layers + 1, s.hidden))
+
+    def embed(self, tokens) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.zeros((len(t), self.shape.hidden), np.int16)
+        check(lib().llmx_model_embed(self.h, t, len(t), out), "embed")
+        return out
+
+    def lm_head_argmax(self, hidden_row, threads=0) -> int:
+        tok = C.c_uint32()
+        check(lib().llmx_model_lm_head_argmax(self.h, np.ascontiguousarray(hidden_row, np.int16).reshape(-1),
+                                              threads, C.byref(tok)), "lm_head_argmax")
+        return tok.value
+
+
+def tp_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().llmx_tp_unique_id(C.cast(buf, C.c_void_p)), "tp_unique_id")
+    return buf.raw
+
+
+class Accelerator:
+    """accelerator_t host:1024-3087 on one B200 (one tensor-parallel rank)."""
+
+    def __init__(self, s: Shape, device=0, tp_rank=0, tp_size=1, tp_id: bytes | None = None):
+        self.shape = s
+        self.h = C.c_void_p()
+        idbuf = C.create_string_buffer(tp_id, 128) if tp_id else None
+        check(lib().llmx_create(C.byref(s), device, tp_rank, tp_size,
+                                C.cast(idbuf, C.c_void_p) if idbuf is not None else None,
+                                C.byref(self.h)), "create")
+
+    def close(self):
+        if self.h:
+            lib().llmx_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def upload_model(self, m: Model):
+        check(lib().llmx_upload_model(self.h, m.h), "upload_model")
+
+    def upload_layer(self, layer, dense):
+        check(lib().llmx_upload_layer(self.h, layer, np.ascontiguousarray(dense, np.int16).reshape(-1)),
+              "upload_layer")
+
+    def upload_norms(self, norms):
+        check(lib().llmx_upload_norms(self.h, np.ascontiguousarray(norms, np.int16).reshape(-1)),
+              "upload_norms")
+
+    def reset_kv(self):
+        check(lib().llmx_reset_kv(self.h), "reset_kv")
+
+    def write_kv(self, layer, position, k, v):
+        """k, v: [kv_heads][count][head_dim] Q8.8 rows of positions [position, position+count)."""
+        k = np.ascontiguousarray(k, np.int16)
+        v = np.ascontiguousarray(v, np.int16)
+        check(lib().llmx_write_kv(self.h, layer, position, k.shape[1], k.reshape(-1), v.reshape(-1)),
+              "write_kv")
+
+    def read_kv(self, layer, position, count):
+        s = self.shape
+        k = np.zeros((s.kv_heads, count, s.head_dim), np.int16)
+        v = np.zeros_like(k)
+        check(lib().llmx_read_kv(self.h, layer, position, count, k.reshape(-1), v.reshape(-1)), "read_kv")
+        return k, v
+
+    def write_hidden(self, pair, rows):
+        rows = np.ascontiguousarray(rows, np.int16)
+        check(lib().llmx_write_hidden(self.h, pair, rows.reshape(-1), rows.shape[0]), "write_hidden")
+
+    def read_hidden(self, pair, nrows):
+        out = np.zeros((nrows, self.shape.hidden), np.int16)
+        check(lib().llmx_read_hidden(self.h, pair, out.reshape(-1), nrows), "read_hidden")
+        return out
+
+    def bind(self, out_pair, in_pair):
+        check(lib().llmx_bind(self.h, out_pair, in_pair), "bind")
+
+    def task(self, op, layer, position, rows, raise_on_error=True):
+        st = Status()
+        rc = lib().llmx_task(self.h, op, layer, position, rows, C.byref(st))
+        if raise_on_error:
+            check(rc, f"task {op}")
+        return rc, st
+
+    def stack(self, hidden, layer_begin=0, layer_count=None, position=0, include_final_norm=True,
+              materialize=True):
+        s = self.shape
+        hidden = np.ascontiguousarray(hidden, np.int16)
+        rows = hidden.shape[0]
+        layer_count = s.layers - layer_begin if layer_count is None else layer_count
+        out = np.zeros((rows, s.hidden), np.int16)
+        st = Status()
+        check(lib().llmx_stack(self.h, hidden.ctypes.data, rows, layer_begin, layer_count, position,
+                               int(include_final_norm), int(materialize), out.ctypes.data, C.byref(st)),
+              "stack")
+        return out if materialize else None
+
+    def stack_async(self, rows, layer_begin, layer_count, position, include_final_norm=True):
+        check(lib().llmx_stack_async(self.h, rows, layer_begin, layer_count, position,
+                                     int(include_final_norm)), "stack_async")
+
+    def synchronize(self):
+        check(lib().llmx_synchronize(self.h), "synchronize")
+
+    @property
+    def stream(self):
+        return lib().llmx_stream(self.h)
+
+    def hidden_ptr(self, pair):
+        return lib().llmx_hidden_device_ptr(self.h, pair)
+
+    @property
+    def kernel_launches(self):
+        return lib().llmx_kernel_launches(self.h)
+
+    @property
+    def device_bytes(self):
+        return lib().llmx_device_bytes(self.h)
+
+
+class Executor:
+    """qwen_executor_t host:7607-8161: embedding + stack + LM head on the host."""
+
+    def __init__(self, acc: Accelerator, model: Model):
+        self.acc, self.model = acc, model
+
+    def run_prompt_block(self, tokens, position, materialize=True):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.zeros((len(t), self.acc.shape.hidden), np.int16)
+        check(lib().llmx_run_prompt_block(self.acc.h, self.model.h, t, len(t), position, int(materialize),
+                                          out.reshape(-1)), "run_prompt_block")
+        return out if materialize else None
+
+    def run_token(self, token, position):
+        out = np.zeros((1, self.acc.shape.hidden), np.int16)
+        check(lib().llmx_run_token(self.acc.h, self.model.h, token, position, out.reshape(-1)), "run_token")
+        return out
