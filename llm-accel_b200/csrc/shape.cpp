@@ -86,8 +86,9 @@ int llmx_shape_validate(const llmx_shape *s) {
     if (s->hidden % s->heads || s->heads % s->kv_heads) return LLMX_ERR_ARG;
     const int hd = s->hidden / s->heads;
     // model_shape_t::validate host:224-236 (even head_dim, GQA group <= 8), plus the
-    // kernels' limits: 128-bit rows (multiples of 8 features), head_dim <= 128.
-    if (hd % 2 || hd > 128 || s->heads / s->kv_heads > 8) return LLMX_ERR_UNSUPPORTED;
+    // kernels' limits: 128-bit rows (multiples of 8 features), head_dim a multiple
+    // of 8 and <= 128.
+    if (hd % 8 || hd > 128 || s->heads / s->kv_heads > 8) return LLMX_ERR_UNSUPPORTED;
     if (s->hidden % 8 || s->inter % 8) return LLMX_ERR_UNSUPPORTED;
     return LLMX_OK;
 }
