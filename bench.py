@@ -1,0 +1,408 @@
+#!/usr/bin/env python3
+"""Decode / prefill tokens per second of the Qwen2.5-3B-shaped fixed-point
+decoder stack (LLM-ACCEL's resident Task 18/19/20 path) on B200.
+
+One step = one single-row decode forward through all 36 layers plus the final
+RMSNorm (run_token, host/host_qwen_8x64.cpp:7665).  The workload is BASELINE
+config 3 on one GPU (512-token prompt as 64 P8 blocks, then decodes at
+positions 512..639) and config 4 under tensor parallelism (2048-token prompt,
+decodes from 2048).  Prefill tok/s of the prompt is reported beside it.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl llmx|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's
+fixed-point oracle (its CPU restatement in oracle/, all host threads) on the
+same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-accel_b200"))
+
+SEED = 20260718
+W_SIGMA = 0.02
+METRIC = "decode tok/s, Qwen2.5-3B-shaped 36-layer fixed-point stack (prefill tok/s, % HBM roofline alongside)"
+CONFIGS = {
+    3: {"prompt": 512, "decodes": 128,
+        "name": "config3: 36-layer Qwen2.5-3B shape, 512-token prompt (64 P8 blocks) + 128 decode forwards, 1 GPU"},
+    4: {"prompt": 2048, "decodes": 256,
+        "name": "config4: 36-layer Qwen2.5-3B shape, 2048-token prompt (256 P8 blocks) + 256 decode forwards, "
+                "tensor parallel"},
+}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = f"/tmp/llmx_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.t0 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            sms.append(sm)
+            maxs.append(mx)
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sms if s > 0.5 * max(sms)]
+        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": max(maxs), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def embed_rows(tokens, hidden):
+    import llmx
+    return np.stack([llmx.gauss_fill(SEED, 0x10, 256.0, hidden, int(t) * hidden) for t in tokens])
+
+
+def bytes_per_decode(shape, world, ctx):
+    """Algorithmic HBM bytes of one decode forward per GPU at context `ctx`
+    (weights once, KV rows read + appended, norm rows, RoPE row, hidden rows)."""
+    H, I, hd, KV = shape.hidden, shape.inter, shape.head_dim, shape.kv_channels
+    w = 2 * (2 * H * H // world + 2 * KV * H + 3 * I * H // world)
+    per_layer = w + 2 * 2 * KV * ctx + 2 * 2 * KV + 2 * 2 * H + 2 * hd + 4 * 2 * H
+    return shape.layers * per_layer + 2 * H * 2
+
+
+def run_llmx(args, cfg_id, world, rank, local, K, W):
+    import torch
+    import llmx
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    cfg = CONFIGS[cfg_id]
+    P = cfg["prompt"]
+    ndec = max(K, W, cfg["decodes"])
+    shape = llmx.shape("qwen2.5-3b", max_seq=P + ndec)
+    H, L = shape.hidden, shape.layers
+    tp_id = None
+    if world > 1:
+        obj = [llmx.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp_id = obj[0]
+    acc = llmx.Accelerator(shape, device=local, tp_rank=rank, tp_size=world, tp_id=tp_id)
+
+    t_setup = time.time()
+    model = None
+    if world == 1:
+        model = llmx.Model(shape).init_gaussian(SEED, W_SIGMA, lm_head=False)
+        acc.upload_model(model)
+    else:  # generate layer by layer (each rank slices its own shard on upload)
+        sizes = [H * H, shape.kv_channels * H, shape.kv_channels * H, H * H, shape.inter * H,
+                 shape.inter * H, H * shape.inter]
+        buf = np.empty(sum(sizes), np.int16)
+        for l in range(L):
+            off = 0
+            for op, n in enumerate(sizes):
+                buf[off:off + n] = llmx.gauss_fill(SEED, 0x1000 + 16 * l + op, W_SIGMA * 4096.0, n)
+                off += n
+            acc.upload_layer(l, buf)
+        acc.upload_norms(np.full((2 * L + 1, H), 256, np.int16))
+    setup_s = time.time() - t_setup
+
+    rng = np.random.default_rng(SEED)
+    prompt = rng.integers(0, shape.vocab, P)
+    dec = rng.integers(0, shape.vocab, ndec)
+    rows = embed_rows(np.concatenate([prompt, dec]), H).astype(np.int16)
+    dev_rows = torch.from_numpy(rows).cuda()
+    stream = torch.cuda.ExternalStream(acc.stream)
+
+    class _Dev:
+        def __init__(self, ptr, shp):
+            self.__cuda_array_interface__ = {"shape": shp, "typestr": "<i2", "data": (ptr, False),
+                                             "version": 3, "strides": None}
+
+    hid1 = torch.as_tensor(_Dev(acc.hidden_ptr(1), (8, H)), device="cuda")
+    launches = [0]
+
+    def prefill():
+        nb = P // 8
+        for b in range(nb):
+            with torch.cuda.stream(stream):
+                hid1[:8].copy_(dev_rows[8 * b:8 * b + 8], non_blocking=True)
+            acc.stack_async(8, 0, L, 8 * b, include_final_norm=(b == nb - 1))
+            launches[0] += acc.kernel_launches
+
+    def decode(i):
+        with torch.cuda.stream(stream):
+            hid1[:1].copy_(dev_rows[P + i:P + i + 1], non_blocking=True)
+        acc.stack_async(1, 0, L, P + i, include_final_norm=True)
+        launches[0] += acc.kernel_launches
+
+    def device_time(fn):
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    clocks = ClockSampler(local)
+    prefill()                                   # warm-up pass: graph capture for 8 rows
+    acc.synchronize()
+    clocks.start()
+    prefill_ms = device_time(prefill)           # timed prefill of the whole prompt
+    for i in range(W):                          # warm-up decodes at positions P..P+W-1
+        decode(i)
+    acc.synchronize()
+    launches[0] = 0
+    decode_ms = device_time(lambda: [decode(i) for i in range(K)])
+    gpu_launches = launches[0]
+    clock = clocks.stop()
+
+    # end to end through the public API: host embedding rows in pinned memory,
+    # H2D, the stack, final norm, D2H of the output row, every step
+    in_p = torch.empty((1, H), dtype=torch.int16).pin_memory()
+    out_p = torch.empty((1, H), dtype=torch.int16).pin_memory()
+    in_np = in_p.numpy()
+    e2e_outputs = []
+
+    def e2e():
+        for i in range(K):
+            in_np[0] = embed_rows([dec[i]], H)[0] if model is None else model.embed([dec[i]])[0]
+            acc.stack_raw(in_p.data_ptr(), 1, 0, L, P + i, True, out_p.data_ptr())
+            if len(e2e_outputs) < 8:
+                e2e_outputs.append(out_p.numpy().copy())
+    t0 = time.time()
+    e2e_ms = device_time(e2e)
+    e2e_wall_ms = (time.time() - t0) * 1e3
+
+    # dominant kernel (Gate/Up + SiLU, ~59% of the decode bytes): mean device time per launch
+    Il = shape.inter // world
+    gu_ms = acc.time_kernel(llmx.KERNEL_GATE_UP, 0, P, 1, 3 * L)
+    down_ms = acc.time_kernel(llmx.KERNEL_DOWN, 0, P, 1, 3 * L)
+    gu_bytes = 2 * Il * H * 2 + H * 2 + H * 2 + Il * 2
+    peak, peak_kind = peaks()
+    gu_gbs = gu_bytes / (gu_ms * 1e-3) / 1e9
+    step_bytes = [bytes_per_decode(shape, world, P + i + 1) for i in range(K)]
+    dec_gbs = sum(step_bytes) / (decode_ms * 1e-3) / 1e9
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(acc, model, shape, rows[P:], P, e2e_outputs)
+
+    result = {
+        "metric": METRIC,
+        "value": K / (decode_ms * 1e-3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": decode_ms / K,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int16",
+        "data": "synthetic: seeded N(0,0.02)->Q4.12 weights, N(0,1)->Q8.8 embedding rows, norm weights 1.0 "
+                "(random-init, no checkpoint)",
+        "config": {"workload": cfg["name"], "layers": L, "hidden": H, "ffn": shape.inter, "heads": shape.heads,
+                   "kv_heads": shape.kv_heads, "prompt_tokens": P,
+                   "decode_positions": [P, P + K - 1], "rows_per_decode": 1, "sequence_batch": 1,
+                   "parallelism": f"tp{world}",
+                   "l2": "no flush: every step streams 5.5 GB/N of weights (>> 126 MB L2)"},
+        "prefill": {"value": P / (prefill_ms * 1e-3), "unit": "tok/s", "ms_per_p8_block": prefill_ms / (P // 8),
+                    "hbm_frac": (P // 8) * bytes_per_decode(shape, world, P // 2) / (prefill_ms * 1e-3) / 1e9
+                    / peak},
+        "decode_roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
+                            "frac": dec_gbs / peak, "bytes_per_step": int(np.mean(step_bytes)),
+                            "peak_source": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": "k_proj<1,EPI_SILU> (RMSNorm + Gate/Up + SiLU x Up, decode)",
+                     "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
+                     "traffic": ncu_traffic("gate_up_decode_ncu.txt"), "bytes_per_launch": gu_bytes,
+                     "ms_per_launch": gu_ms, "down_ms_per_launch": down_ms, "peak_source": peak_kind},
+        "e2e": {"value": K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
+                "d2h_bytes_per_step": H * 2, "wall_ms_per_step": e2e_wall_ms / K,
+                "api": "llmx_stack (run_token boundary: host embedding row -> H2D -> 36x Task18/19 -> Task20 -> D2H)"},
+        "gpu_launches": gpu_launches,
+        "clocks": clock,
+        "setup_s": setup_s,
+    }
+    if cpu is not None:
+        result["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    acc.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(acc, model, shape, dec_rows, P, gpu_outputs):
+    """The oracle restatement (1 thread) on a bounded sample of the same workload:
+    decode forwards at positions P.. from the device's KV cache state; checks
+    the oracle's outputs against the device outputs of the same steps."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle as O
+    from helpers import OracleState, oracle_shape
+
+    O.set_exp_mode(O.EXP_TRUNC)
+    O.set_threads(1)
+    L = shape.layers
+    ref = OracleState(O, oracle_shape(O, shape), [model.layer(l) for l in range(L)], model.norms())
+    for l in range(L):
+        k, v = acc.read_kv(l, 0, P)
+        ref.kc[l][:, :P] = k
+        ref.vc[l][:, :P] = v
+    n, t0, same = 0, time.time(), True
+    while n < min(8, len(gpu_outputs)) and (time.time() - t0) < 20.0:
+        out = ref.stack(dec_rows[n:n + 1], P + n)
+        same &= bool(np.array_equal(out, gpu_outputs[n]))
+        n += 1
+    dt = time.time() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"{n} decode forwards (36 layers + final norm) at positions {P}..{P + n - 1} from the "
+                      f"device KV state, integer oracle restatement, 1 thread",
+            "matches_gpu": same}
+
+
+def run_reference(args, cfg_id, world, K, W):
+    """The reference's fixed-point golden model (CPU restatement, all host
+    threads) on the same workload: decode forwards at positions P.. over a
+    seeded KV cache."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle as O
+    from helpers import OracleState
+
+    cores = len(os.sched_getaffinity(0))
+    O.set_exp_mode(O.EXP_TRUNC)
+    O.set_threads(cores)
+    cfg = CONFIGS[cfg_id]
+    P = cfg["prompt"]
+    ndec = max(K, W, cfg["decodes"])
+    s = O.shape("qwen2.5-3b", max_seq=P + ndec)
+    L = s.layers
+    layers = [O.gaussian_layer(s, SEED, l, W_SIGMA) for l in range(L)]
+    norms = np.full((2 * L + 1, s.hidden), 256, np.int16)
+    ref = OracleState(O, s, layers, norms)
+    rng = np.random.default_rng(SEED + 1)
+    for l in range(L):  # seeded KV state for positions < P (decode cost does not depend on values)
+        ref.kc[l][:, :P] = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767)
+        ref.vc[l][:, :P] = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767)
+    dec = np.random.default_rng(SEED).integers(0, s.vocab, P + ndec)[P:]
+    rows = O.gaussian_embedding_rows(s, SEED, dec[:max(K, W)])
+    t0 = time.time()
+    for i in range(W):
+        ref.stack(rows[i:i + 1], P + i)
+    per_step = (time.time() - t0) / W
+    if K * per_step > 150.0:  # bounded CPU sample: keep the whole run within a few minutes
+        K = max(3, int(150.0 / per_step))
+    t0 = time.time()
+    for i in range(K):
+        ref.stack(rows[i:i + 1], P + i)
+    dt = time.time() - t0
+    v = K / dt
+    print(json.dumps({
+        "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": dt * 1e3 / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int16", "data": "synthetic (same seeds as the llmx arm)",
+        "config": {"workload": CONFIGS[cfg_id]["name"], "prompt_tokens": P, "decode_positions": [P, P + K - 1]},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{K} decode forwards (36 layers + final norm) at positions {P}..{P + K - 1}, "
+                                   f"oracle restatement of the reference golden model, {cores} threads"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["llmx", "reference"], default="llmx")
+    ap.add_argument("--config", type=int, choices=[3, 4], default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg_id = args.config or (3 if world == 1 else 4)
+    K = args.steps if args.steps is not None else CONFIGS[cfg_id]["decodes"]
+    W = max(3, args.warmup)
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        return run_reference(args, cfg_id, world, K, W)
+    return run_llmx(args, cfg_id, world, rank, local, K, W)
+
+
+if __name__ == "__main__":
+    sys.exit(main() or 0)

@@ -212,6 +212,23 @@ uint64_t llmx_kernel_launches(const llmx_ctx *ctx);
 /* Bytes of device memory the context holds. */
 uint64_t llmx_device_bytes(const llmx_ctx *ctx);
 
+/* Kernels of the path, for per-kernel timing (no reference counterpart: the
+ * reference reads its CU running times from the XRT profile_kernels.csv,
+ * scripts/report_hwemu_kernel_cycles.sh:25-38). */
+#define LLMX_KERNEL_QKV 0         /* RMSNorm + Q/K/V + RoPE + KV append */
+#define LLMX_KERNEL_ATTN_SCORES 1 /* QK scores + tile maxima */
+#define LLMX_KERNEL_ATTN_PV 2     /* probabilities + PV + tile combine */
+#define LLMX_KERNEL_O 3           /* O projection + residual */
+#define LLMX_KERNEL_GATE_UP 4     /* RMSNorm + Gate/Up + SiLU x Up */
+#define LLMX_KERNEL_DOWN 5        /* Down projection + residual */
+#define LLMX_KERNEL_FINAL_NORM 6
+/* Launch one kernel of the path `iters` times back to back on the context
+ * stream (operating on whatever the buffers hold; launch i uses layer
+ * (layer + i) mod layers so consecutive launches stream distinct weights)
+ * between two CUDA events and return the mean device time per launch in ms. */
+int llmx_time_kernel(llmx_ctx *ctx, int kernel, uint32_t layer, uint32_t position,
+                     uint32_t rows, int iters, double *ms_per_launch);
+
 /* ---------------------------------------------------------------------------
  * Host runtime: qwen_executor_t host:7607-8161
  * ------------------------------------------------------------------------- */

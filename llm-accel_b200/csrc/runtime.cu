@@ -126,6 +126,99 @@ int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *res
     return LLMX_OK;
 }
 
+// Kernel-level pieces of the coarse tasks (ids of LLMX_KERNEL_*).
+ProjArgs qkv_args(llmx_ctx *c, uint32_t layer, const int16_t *in) {
+    const llmx_shape &s = c->s;
+    ProjArgs a{};
+    a.w = wl(c, layer);
+    a.K = s.hidden;
+    a.npairs = (c->Hq + 2 * c->KV) / 2;
+    a.x = in;
+    a.norm = c->norms + (size_t)2 * layer * s.hidden;
+    a.inv_elems = c->inv_elems;
+    a.inv_rms_const = c->inv_rms_const;
+    a.step = c->step;
+    a.out = c->q;
+    a.out_stride = c->Hq;
+    a.kc = kc_layer(c, layer);
+    a.vc = vc_layer(c, layer);
+    a.rope = c->rope;
+    a.hd = c->hd;
+    a.q_pairs = c->Hq / 2;
+    a.kv_pairs = c->KV / 2;
+    a.max_seq = s.max_seq;
+    return a;
+}
+
+AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
+    AttnArgs t{};
+    t.q = c->q;
+    t.kc = kc_layer(c, layer);
+    t.vc = vc_layer(c, layer);
+    t.scores = c->scores;
+    t.tmax = c->tmax;
+    t.tval = c->tval;
+    t.tsum = c->tsum;
+    t.told = c->told;
+    t.tickets = c->tickets;
+    t.out = c->att;
+    t.ptab = c->ptab;
+    t.step = c->step;
+    t.q_heads = c->hq;
+    t.group = std::min(c->G, c->hq);
+    t.kv_first = c->h0 / c->G;
+    t.hd = c->hd;
+    t.max_seq = c->s.max_seq;
+    t.max_tiles = c->max_tiles;
+    t.qk_scale = c->qk_scale;
+    return t;
+}
+
+ProjArgs o_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in) {
+    ProjArgs o{};
+    o.w = wl(c, layer) + c->w_qkv;
+    o.K = c->Hq;
+    o.npairs = c->s.hidden / 2;
+    o.x = c->att;
+    o.step = c->step;
+    o.out = out;
+    o.out_stride = c->s.hidden;
+    o.resid = in;
+    o.partial = c->partial;
+    return o;
+}
+
+ProjArgs gu_args(llmx_ctx *c, uint32_t layer, const int16_t *in) {
+    const llmx_shape &s = c->s;
+    ProjArgs g{};
+    g.w = wl(c, layer) + c->w_qkv + c->w_o;
+    g.K = s.hidden;
+    g.npairs = c->Il;
+    g.x = in;
+    g.norm = c->norms + (size_t)(2 * layer + 1) * s.hidden;
+    g.inv_elems = c->inv_elems;
+    g.inv_rms_const = c->inv_rms_const;
+    g.step = c->step;
+    g.out = c->act;
+    g.out_stride = c->Il;
+    g.etab = c->etab;
+    return g;
+}
+
+ProjArgs down_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in) {
+    ProjArgs d{};
+    d.w = wl(c, layer) + c->w_qkv + c->w_o + c->w_gu;
+    d.K = c->Il;
+    d.npairs = c->s.hidden / 2;
+    d.x = c->act;
+    d.step = c->step;
+    d.out = out;
+    d.out_stride = c->s.hidden;
+    d.resid = in;
+    d.partial = c->partial;
+    return d;
+}
+
 // Enqueue the kernels of one coarse task on the context stream.
 int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32_t in_pair,
                  uint32_t out_pair) {
@@ -133,89 +226,23 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     const int rt = rows_template(rows);
     const int16_t *in = c->hid[in_pair];
     int16_t *out = c->hid[out_pair];
+    const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
-        ProjArgs a{};
-        a.w = wl(c, layer);
-        a.K = s.hidden;
-        a.npairs = (c->Hq + 2 * c->KV) / 2;
-        a.x = in;
-        a.norm = c->norms + (size_t)2 * layer * s.hidden;
-        a.inv_elems = c->inv_elems;
-        a.inv_rms_const = c->inv_rms_const;
-        a.step = c->step;
-        a.out = c->q;
-        a.out_stride = c->Hq;
-        a.kc = kc_layer(c, layer);
-        a.vc = vc_layer(c, layer);
-        a.rope = c->rope;
-        a.hd = c->hd;
-        a.q_pairs = c->Hq / 2;
-        a.kv_pairs = c->KV / 2;
-        a.max_seq = s.max_seq;
+        const ProjArgs a = qkv_args(c, layer, in);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
-        AttnArgs t{};
-        t.q = c->q;
-        t.kc = kc_layer(c, layer);
-        t.vc = vc_layer(c, layer);
-        t.scores = c->scores;
-        t.tmax = c->tmax;
-        t.tval = c->tval;
-        t.tsum = c->tsum;
-        t.told = c->told;
-        t.tickets = c->tickets;
-        t.out = c->att;
-        t.ptab = c->ptab;
-        t.step = c->step;
-        t.q_heads = c->hq;
-        t.group = std::min(c->G, c->hq);
-        t.kv_first = c->h0 / c->G;
-        t.hd = c->hd;
-        t.max_seq = s.max_seq;
-        t.max_tiles = c->max_tiles;
-        t.qk_scale = c->qk_scale;
+        const AttnArgs t = attn_args(c, layer);
         CK(launch_attn_scores(t, (int)rows, c->stream));
         CK(launch_attn_pv(t, (int)rows, c->stream));
-        ProjArgs o{};
-        o.w = wl(c, layer) + c->w_qkv;
-        o.K = c->Hq;
-        o.npairs = s.hidden / 2;
-        o.x = c->att;
-        o.step = c->step;
-        o.out = out;
-        o.out_stride = s.hidden;
-        o.resid = in;
-        o.partial = c->partial;
-        const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+        const ProjArgs o = o_args(c, layer, out, in);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
         c->launches += 4;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
         return LLMX_OK;
     }
     if (op == LLMX_OP_FFN_SUBLAYER) {
-        ProjArgs g{};
-        g.w = wl(c, layer) + c->w_qkv + c->w_o;
-        g.K = s.hidden;
-        g.npairs = c->Il;
-        g.x = in;
-        g.norm = c->norms + (size_t)(2 * layer + 1) * s.hidden;
-        g.inv_elems = c->inv_elems;
-        g.inv_rms_const = c->inv_rms_const;
-        g.step = c->step;
-        g.out = c->act;
-        g.out_stride = c->Il;
-        g.etab = c->etab;
+        const ProjArgs g = gu_args(c, layer, in);
         CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
-        ProjArgs d{};
-        d.w = wl(c, layer) + c->w_qkv + c->w_o + c->w_gu;
-        d.K = c->Il;
-        d.npairs = s.hidden / 2;
-        d.x = c->act;
-        d.step = c->step;
-        d.out = out;
-        d.out_stride = s.hidden;
-        d.resid = in;
-        d.partial = c->partial;
-        const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+        const ProjArgs d = down_args(c, layer, out, in);
         CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
         c->launches += 2;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
@@ -606,6 +633,67 @@ int llmx_synchronize(llmx_ctx *c) {
     if (!c) return LLMX_ERR_ARG;
     CK(cudaSetDevice(c->dev));
     CK(cudaStreamSynchronize(c->stream));
+    return LLMX_OK;
+}
+
+int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position, uint32_t rows, int iters,
+                     double *ms_per_launch) {
+    if (!c || !ms_per_launch || iters < 1 || rows == 0 || rows > LLMX_MAX_ROWS ||
+        layer >= (uint32_t)c->s.layers || position + rows > (uint32_t)c->s.max_seq)
+        return LLMX_ERR_ARG;
+    if (!model_ready(c, 0, (uint32_t)c->s.layers)) return LLMX_ERR_STATE;
+    CK(cudaSetDevice(c->dev));
+    const int rt = rows_template(rows);
+    const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+    int16_t *out = c->hid[0];
+    const int16_t *in = c->hid[1];
+    int rc = set_step(c, position, rows);
+    if (rc) return rc;
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    uint32_t cur = layer;  // rotate layers so that repeated launches stream distinct weights
+    auto one = [&]() -> cudaError_t {
+        const uint32_t layer = cur;
+        cur = (cur + 1) % (uint32_t)c->s.layers;
+        switch (kernel) {
+        case LLMX_KERNEL_QKV: {
+            const ProjArgs a = qkv_args(c, layer, in);
+            return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
+        }
+        case LLMX_KERNEL_ATTN_SCORES: return launch_attn_scores(attn_args(c, layer), (int)rows, c->stream);
+        case LLMX_KERNEL_ATTN_PV: return launch_attn_pv(attn_args(c, layer), (int)rows, c->stream);
+        case LLMX_KERNEL_O: {
+            const ProjArgs o = o_args(c, layer, out, in);
+            return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
+        }
+        case LLMX_KERNEL_GATE_UP: {
+            const ProjArgs g = gu_args(c, layer, in);
+            return launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream);
+        }
+        case LLMX_KERNEL_DOWN: {
+            const ProjArgs d = down_args(c, layer, out, in);
+            return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
+        }
+        case LLMX_KERNEL_FINAL_NORM: {
+            NormArgs n{in, c->norms + (size_t)2 * c->s.layers * c->s.hidden, out, c->s.hidden, c->inv_elems,
+                       c->inv_rms_const, c->step};
+            return launch_rmsnorm(n, (int)rows, c->stream);
+        }
+        default: return cudaErrorInvalidValue;
+        }
+    };
+    cudaError_t e = one();  // warm-up launch
+    if (e == cudaSuccess) e = cudaEventRecord(e0, c->stream);
+    for (int i = 0; i < iters && e == cudaSuccess; i++) e = one();
+    if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return fail_cuda(e, "llmx_time_kernel");
+    *ms_per_launch = (double)ms / iters;
     return LLMX_OK;
 }
 

@@ -26,6 +26,7 @@ BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 
 ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED = range(100, 108)
 OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
 MAX_ROWS = 8
+KERNEL_QKV, KERNEL_ATTN_SCORES, KERNEL_ATTN_PV, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(7)
 
 
 class LlmxError(RuntimeError):
@@ -116,6 +117,8 @@ def lib():
             "llmx_hidden_device_ptr": (vp, [vp, C.c_uint32]),
             "llmx_kernel_launches": (C.c_uint64, [vp]),
             "llmx_device_bytes": (C.c_uint64, [vp]),
+            "llmx_time_kernel": (C.c_int, [vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int,
+                                           C.POINTER(C.c_double)]),
             "llmx_run_prompt_block": (C.c_int, [vp, vp, u32p, C.c_uint32, C.c_uint32, C.c_int, i16p]),
             "llmx_run_token": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, i16p]),
         }
@@ -320,6 +323,20 @@ class Accelerator:
                                int(include_final_norm), int(materialize), out.ctypes.data, C.byref(st)),
               "stack")
         return out if materialize else None
+
+    def stack_raw(self, in_ptr, rows, layer_begin, layer_count, position, include_final_norm=True,
+                  out_ptr=None):
+        """llmx_stack on caller-owned host buffers (e.g. pinned memory)."""
+        st = Status()
+        check(lib().llmx_stack(self.h, in_ptr, rows, layer_begin, layer_count, position,
+                               int(include_final_norm), int(out_ptr is not None), out_ptr, C.byref(st)),
+              "stack")
+
+    def time_kernel(self, kernel, layer, position, rows, iters):
+        ms = C.c_double()
+        check(lib().llmx_time_kernel(self.h, kernel, layer, position, rows, iters, C.byref(ms)),
+              "time_kernel")
+        return ms.value
 
     def stack_async(self, rows, layer_begin, layer_count, position, include_final_norm=True):
         check(lib().llmx_stack_async(self.h, rows, layer_begin, layer_count, position,

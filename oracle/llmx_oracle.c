@@ -187,17 +187,44 @@ static inline int16_t round_mac_total(int64_t s) {
     return sat16(rnd64(accum, 8));
 }
 
-void orc_projection(const int16_t *x, int rows, int in_dim, const int16_t *w,
-                    int out_dim, int16_t *y) {
-    for (int r = 0; r < rows; r++) {
-        const int16_t *xr = x + (size_t)r * in_dim;
-        for (int o = 0; o < out_dim; o++) {
-            const int16_t *wr = w + (size_t)o * in_dim;
+static int g_threads = 1;
+void orc_set_threads(int n) { g_threads = n < 1 ? 1 : (n > 256 ? 256 : n); }
+
+typedef struct {
+    const int16_t *x, *w;
+    int16_t *y;
+    int rows, in_dim, out_dim, o_begin, o_end;
+} proj_job_t;
+
+static void *proj_worker(void *arg) {
+    const proj_job_t *j = (const proj_job_t *)arg;
+    for (int o = j->o_begin; o < j->o_end; o++) {
+        const int16_t *wr = j->w + (size_t)o * j->in_dim;
+        for (int r = 0; r < j->rows; r++) {
+            const int16_t *xr = j->x + (size_t)r * j->in_dim;
             int64_t s = 0;
-            for (int i = 0; i < in_dim; i++) s += (int32_t)xr[i] * (int32_t)wr[i];
-            y[(size_t)r * out_dim + o] = round_mac_total(s);
+            for (int i = 0; i < j->in_dim; i++) s += (int32_t)xr[i] * (int32_t)wr[i];
+            j->y[(size_t)r * j->out_dim + o] = round_mac_total(s);
         }
     }
+    return NULL;
+}
+
+/* Rows x out_dim exact dot products; output features split over g_threads. */
+void orc_projection(const int16_t *x, int rows, int in_dim, const int16_t *w,
+                    int out_dim, int16_t *y) {
+    int t = g_threads;
+    if ((int64_t)out_dim * in_dim * rows < (1 << 22) || t > out_dim) t = 1;
+    proj_job_t jobs[256];
+    pthread_t tid[256];
+    for (int i = 0; i < t; i++) {
+        jobs[i] = (proj_job_t){x, w, y, rows, in_dim, out_dim, (int)((int64_t)out_dim * i / t),
+                               (int)((int64_t)out_dim * (i + 1) / t)};
+        if (t == 1) proj_worker(&jobs[0]);
+        else pthread_create(&tid[i], NULL, proj_worker, &jobs[i]);
+    }
+    if (t > 1)
+        for (int i = 0; i < t; i++) pthread_join(tid[i], NULL);
 }
 
 /* Exact integer partial dot products over input columns [k_begin, k_end):
@@ -726,20 +753,44 @@ int orc_gauss_table(double sigma_raw, uint64_t *thresholds, int max_entries, int
     return n;
 }
 
+typedef struct {
+    const uint64_t *tab;
+    int cnt, kmin;
+    uint64_t key, index0;
+    int16_t *out;
+    size_t begin, end;
+} gauss_job_t;
+
+static void *gauss_worker(void *arg) {
+    const gauss_job_t *j = (const gauss_job_t *)arg;
+    for (size_t i = j->begin; i < j->end; i++) {
+        const uint64_t u = mix64(j->key + j->index0 + i) >> 32;
+        int lo = 0, hi = j->cnt - 1; /* smallest index with u < tab[index] */
+        while (lo < hi) {
+            const int mid = (lo + hi) / 2;
+            if (u < j->tab[mid]) hi = mid;
+            else lo = mid + 1;
+        }
+        j->out[i] = (int16_t)(lo + j->kmin);
+    }
+    return NULL;
+}
+
 void orc_gauss_fill(uint64_t seed, uint64_t stream, double sigma_raw,
                     uint64_t index0, int16_t *out, size_t n) {
-    static uint64_t tab[65536];
+    uint64_t *tab = (uint64_t *)malloc(sizeof(uint64_t) * 65536);
     int kmin = 0;
     const int cnt = orc_gauss_table(sigma_raw, tab, 65536, &kmin);
     const uint64_t key = mix64(seed ^ (stream * 0xD1B54A32D192ED03ull));
-    for (size_t i = 0; i < n; i++) {
-        const uint64_t u = mix64(key + index0 + i) >> 32;
-        int lo = 0, hi = cnt - 1; /* smallest j with u < tab[j] */
-        while (lo < hi) {
-            const int mid = (lo + hi) / 2;
-            if (u < tab[mid]) hi = mid;
-            else lo = mid + 1;
-        }
-        out[i] = (int16_t)(lo + kmin);
+    int t = n < (1u << 20) ? 1 : g_threads;
+    gauss_job_t jobs[256];
+    pthread_t tid[256];
+    for (int i = 0; i < t; i++) {
+        jobs[i] = (gauss_job_t){tab, cnt, kmin, key, index0, out, n * i / t, n * (i + 1) / t};
+        if (t == 1) gauss_worker(&jobs[0]);
+        else pthread_create(&tid[i], NULL, gauss_worker, &jobs[i]);
     }
+    if (t > 1)
+        for (int i = 0; i < t; i++) pthread_join(tid[i], NULL);
+    free(tab);
 }

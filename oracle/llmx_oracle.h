@@ -58,6 +58,7 @@ int16_t orc_prob(int16_t x);       /* golden_attention_probability host:588-596 
 int16_t orc_inv_rms_const(int32_t n); /* inv_rms when recip(fm(n)) == 0 */
 
 /* ---- tensor ops (row-major int16) ---------------------------------------- */
+void orc_set_threads(int n); /* host threads for the projections (default 1) */
 void orc_projection(const int16_t *x, int rows, int in_dim, const int16_t *w,
                     int out_dim, int16_t *y);
 void orc_projection_partial(const int16_t *x, int rows, int in_dim,

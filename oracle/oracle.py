@@ -81,6 +81,7 @@ def lib():
             "orc_set_exp_mode": (None, [C.c_int]),
             "orc_get_exp_mode": (C.c_int, []),
             "orc_set_tables": (None, [i16p, i16p]),
+            "orc_set_threads": (None, [C.c_int]),
             "orc_recip": (C.c_int16, [C.c_int16]),
             "orc_rsqrt": (C.c_int16, [C.c_int32]),
             "orc_silu": (C.c_int16, [C.c_int16]),
@@ -129,6 +130,10 @@ def _c16(a):
 # ---------------------------------------------------------------------------
 def set_exp_mode(mode: int):
     lib().orc_set_exp_mode(mode)
+
+
+def set_threads(n: int):
+    lib().orc_set_threads(n)
 
 
 def set_tables(e16, p18):
@@ -292,3 +297,17 @@ def gauss_table(sigma_raw):
     kmin = C.c_int(0)
     n = lib().orc_gauss_table(sigma_raw, t, 65536, C.byref(kmin))
     return t[:n].copy(), kmin.value
+
+
+def gaussian_layer(s: Shape, seed: int, layer: int, w_sigma: float = 0.02):
+    """Dense blob of layer `layer` of the synthetic benchmark model (Q,K,V,O,
+    Gate,Up,Down from streams 0x1000 + 16*layer + op, N(0, w_sigma) in Q4.12)."""
+    H, I, KV = s.hidden, s.inter, s.kv_channels
+    sizes = [H * H, KV * H, KV * H, H * H, I * H, I * H, H * I]
+    return np.concatenate([gauss_fill(seed, 0x1000 + 16 * layer + op, w_sigma * 4096.0, n)
+                           for op, n in enumerate(sizes)])
+
+
+def gaussian_embedding_rows(s: Shape, seed: int, tokens):
+    """Embedding rows of the synthetic model: N(0, 1) in Q8.8, stream 0x10."""
+    return np.stack([gauss_fill(seed, 0x10, 256.0, s.hidden, int(t) * s.hidden) for t in tokens])
