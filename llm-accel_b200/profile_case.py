@@ -1,0 +1,68 @@
+"""Small, self-contained profiling case for the path's kernels.
+
+Builds a Qwen2.5-3B-shaped stack with a few layers (synthetic N(0,0.02)
+weights), preloads a seeded KV cache to `--position`, then
+  --table : prints the mean device time of every kernel (llmx_time_kernel,
+            CUDA events on the context stream) for 1-row decode and 8-row blocks;
+  --eager : runs `--steps` eager Task 18/19/20 sequences (no CUDA graph) so that a
+            profiler sees plain launches (ncu -k regex:... -c ...).
+Usage: python llm-accel_b200/profile_case.py --layers 4 --position 512 --table
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import llmx  # noqa: E402
+
+NAMES = ["qkv", "attn_scores", "attn_pv", "o_proj", "gate_up", "down", "final_norm"]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--position", type=int, default=512)
+    ap.add_argument("--max-seq", type=int, default=2304)
+    ap.add_argument("--table", action="store_true")
+    ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--rows", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--iters", type=int, default=40)
+    args = ap.parse_args()
+    s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq)
+    m = llmx.Model(s).init_gaussian(20260718, 0.02)
+    acc = llmx.Accelerator(s)
+    acc.upload_model(m)
+    rng = np.random.default_rng(0)
+    P = args.position
+    for l in range(s.layers):
+        k = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
+        v = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
+        acc.write_kv(l, 0, k, v)
+    acc.write_hidden(1, m.embed(rng.integers(0, s.vocab, 8)))
+    if args.table:
+        out = {}
+        for rows in (1, 8):
+            out[f"rows{rows}"] = {n: acc.time_kernel(i, 0, P, rows, args.iters) * 1e3 for i, n in enumerate(NAMES)}
+        print(json.dumps({"position": P, "layers": s.layers, "us_per_launch": out}, indent=1))
+    if args.eager:
+        for step in range(args.steps):
+            pos = P + step * args.rows
+            for l in range(s.layers):
+                acc.bind(0, 1)
+                acc.task(llmx.OP_ATTENTION, l, pos, args.rows)
+                acc.bind(1, 0)
+                acc.task(llmx.OP_FFN, l, pos, args.rows)
+            acc.bind(0, 1)
+            acc.task(llmx.OP_FINAL_NORM, 0, pos, args.rows)
+        print("eager steps done")
+    acc.close()
+
+
+if __name__ == "__main__":
+    main()
