@@ -215,13 +215,12 @@ uint64_t llmx_device_bytes(const llmx_ctx *ctx);
 /* Kernels of the path, for per-kernel timing (no reference counterpart: the
  * reference reads its CU running times from the XRT profile_kernels.csv,
  * scripts/report_hwemu_kernel_cycles.sh:25-38). */
-#define LLMX_KERNEL_QKV 0         /* RMSNorm + Q/K/V + RoPE + KV append */
-#define LLMX_KERNEL_ATTN_SCORES 1 /* QK scores + tile maxima */
-#define LLMX_KERNEL_ATTN_PV 2     /* probabilities + PV + tile combine */
-#define LLMX_KERNEL_O 3           /* O projection + residual */
-#define LLMX_KERNEL_GATE_UP 4     /* RMSNorm + Gate/Up + SiLU x Up */
-#define LLMX_KERNEL_DOWN 5        /* Down projection + residual */
-#define LLMX_KERNEL_FINAL_NORM 6
+#define LLMX_KERNEL_QKV 0        /* RMSNorm + Q/K/V + RoPE + KV append */
+#define LLMX_KERNEL_ATTN 1       /* tile-exact online-softmax attention */
+#define LLMX_KERNEL_O 2          /* O projection + residual */
+#define LLMX_KERNEL_GATE_UP 3    /* RMSNorm + Gate/Up + SiLU x Up */
+#define LLMX_KERNEL_DOWN 4       /* Down projection + residual */
+#define LLMX_KERNEL_FINAL_NORM 5
 /* Launch one kernel of the path `iters` times back to back on the context
  * stream (operating on whatever the buffers hold; launch i uses layer
  * (layer + i) mod layers so consecutive launches stream distinct weights)

@@ -12,53 +12,14 @@
 // tensor-parallel all-reduce.  RMSNorm (kernel/compute_stream.cpp:227-288) is
 // the prologue that stages the activations in shared memory.
 //
-// Attention (run_cc8_resident_decode_attention kernel/control_cache_8x64.cpp:5492-5765)
-// keeps the reference's 64-position tile recurrence bit-exact while running
-// tiles in parallel: pass 1 writes per-tile QK scores and tile maxima; pass 2
-// recomputes the running max of each tile as a prefix max, produces the tile's
-// Q2.14 probabilities, tile sum and PV tile value, and the last CTA of a
-// (row, KV head) replays the cheap Q16.16 rescale/accumulate recurrence over
-// tiles in order and finalises.  Scores never leave L2-sized scratch.
+// Attention lives in attention.cu.
 #include <cuda_runtime.h>
 
+#include "device_util.cuh"
 #include "fixed.cuh"
 #include "kernels.cuh"
 
 namespace llmx {
-
-// --------------------------------------------------------------------------
-// small device helpers
-// --------------------------------------------------------------------------
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-// a: two signed int16 (low half = even k); b: bytes; .lo uses bytes 0,1 (unsigned)
-__device__ __forceinline__ int dp2a_lo_su(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-// .hi uses bytes 2,3 (signed)
-__device__ __forceinline__ int dp2a_hi_ss(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ int32_t add_sat(int32_t a, int32_t b) {
-    int32_t d;
-    asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ int64_t shfl_xor64(int64_t v, int o) {
-    return __shfl_xor_sync(0xffffffffu, v, o);
-}
 
 // golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
 // then x up with one rounding (stream_silu_mul :123-164).
@@ -200,8 +161,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_proj(const ProjArgs a) {
     // before waiting for it (programmatic dependent launch).
     bool preloaded = p < a.npairs;
     if (preloaded) load_chunk(p, 0);
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const Step st = *a.step;
     const int rows = st.rows;
     stage_rows<R>(a, xs, rows);
@@ -371,187 +332,7 @@ int proj_max_ctas_per_sm(int epi, int rows_tmpl, int K) {
     }
 }
 
-// --------------------------------------------------------------------------
-// attention pass 1: QK scores of one 64-position tile for the query heads of
-// one KV head (golden_attention_mm host:3219-3278 with scale_qk)
-// --------------------------------------------------------------------------
-constexpr int kKvStride = 136;  // padded smem row (int16) -> conflict-free 128-bit reads
-constexpr int kAttnThreads = 256;
-constexpr int kMaxHd = 128;
-constexpr int kMaxGroup = 8;
-
-__global__ void __launch_bounds__(kAttnThreads) k_attn_scores(const AttnArgs a) {
-    __shared__ __align__(16) int16_t ks[kTile * kKvStride];
-    __shared__ __align__(16) int16_t qs[kMaxGroup * kMaxHd];
-    __shared__ int32_t hmax[kMaxGroup][kAttnThreads / 32];
-    pdl_trigger();
-    pdl_wait();
-    const Step st = *a.step;
-    const int r = blockIdx.z, slot = blockIdx.y, t = blockIdx.x;
-    if (r >= st.rows) return;
-    const int ctx = st.position + r + 1;
-    const int ntiles = (ctx + kTile - 1) / kTile;
-    if (t >= ntiles) return;
-    const int p0 = t * kTile;
-    const int tl = min(kTile, ctx - p0);
-    const int hd = a.hd, G = a.group;
-    const int kvh = a.kv_first + slot;  // KV heads are replicated on every rank
-    const int16_t *kbase = a.kc + ((size_t)kvh * a.max_seq + p0) * hd;
-    // K tile -> Q4.12 with saturation (golden_weight_t(fm))
-    for (int i = threadIdx.x; i < tl * hd; i += blockDim.x) {
-        const int p = i / hd, e = i - p * hd;
-        ks[p * kKvStride + e] = (int16_t)sat16((int32_t)kbase[(size_t)p * hd + e] * 16);
-    }
-    const int16_t *qbase = a.q + (size_t)r * a.q_heads * hd + (size_t)slot * G * hd;
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qbase[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int32_t local_max[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; h++) local_max[h] = -32768;
-    for (int i = threadIdx.x; i < G * kTile; i += blockDim.x) {
-        const int h = i / kTile, p = i - h * kTile;
-        if (p >= tl) continue;
-        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
-        const int16_t *qv = qs + h * hd;
-        const int16_t *kv = ks + p * kKvStride;
-        for (int e = 0; e < hd; e += 4) {
-            // per-product rounding to Q16.16, four saturating banks (k mod 4)
-            b0 = add_sat(b0, (int32_t)rnd((int32_t)qv[e] * (int32_t)kv[e], 4));
-            b1 = add_sat(b1, (int32_t)rnd((int32_t)qv[e + 1] * (int32_t)kv[e + 1], 4));
-            b2 = add_sat(b2, (int32_t)rnd((int32_t)qv[e + 2] * (int32_t)kv[e + 2], 4));
-            b3 = add_sat(b3, (int32_t)rnd((int32_t)qv[e + 3] * (int32_t)kv[e + 3], 4));
-        }
-        int32_t tot = sat32((int64_t)b0 + b1 + b2 + b3);
-        tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));
-        const int32_t sc = sat16(rnd(tot, 8));
-        a.scores[((size_t)r * a.q_heads + slot * G + h) * a.max_seq + p0 + p] = (int16_t)sc;
-#pragma unroll
-        for (int hh = 0; hh < kMaxGroup; hh++)
-            if (hh == h) local_max[hh] = max(local_max[hh], sc);
-    }
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; h++) {
-        int32_t m = local_max[h];
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) hmax[h][warp] = m;
-    }
-    __syncthreads();
-    if (threadIdx.x < G) {
-        int32_t m = -32768;
-        for (int w = 0; w < kAttnThreads / 32; w++) m = max(m, hmax[threadIdx.x][w]);
-        a.tmax[((size_t)r * a.q_heads + slot * G + threadIdx.x) * a.max_tiles + t] = (int16_t)m;
-    }
-}
-
-// --------------------------------------------------------------------------
-// attention pass 2: probabilities, tile sum, PV of one tile; the last CTA of
-// a (row, KV head) combines the tiles in order and finalises
-// (golden_tiled_flash_attention_q2_14_impl<true> host:3610-3739)
-// --------------------------------------------------------------------------
-__global__ void __launch_bounds__(kAttnThreads) k_attn_pv(const AttnArgs a) {
-    __shared__ __align__(16) int16_t vs[kTile * kKvStride];
-    __shared__ int16_t ps[kMaxGroup][kTile];
-    __shared__ int32_t mcur[kMaxGroup], mprev[kMaxGroup];
-    __shared__ int32_t tsum_s[kMaxGroup];
-    __shared__ uint32_t ticket_s;
-    pdl_trigger();
-    pdl_wait();
-    const Step st = *a.step;
-    const int r = blockIdx.z, slot = blockIdx.y, t = blockIdx.x;
-    if (r >= st.rows) return;
-    const int ctx = st.position + r + 1;
-    const int ntiles = (ctx + kTile - 1) / kTile;
-    if (t >= ntiles) return;
-    const int p0 = t * kTile;
-    const int tl = min(kTile, ctx - p0);
-    const int hd = a.hd, G = a.group;
-    const size_t hrow = (size_t)r * a.q_heads + (size_t)slot * G;  // first local head row
-
-    if (threadIdx.x < G) {
-        // running max after tile t and before it (m_{-1} = fm(-128))
-        const int16_t *tm = a.tmax + (hrow + threadIdx.x) * a.max_tiles;
-        int32_t mp = -32768;
-        for (int u = 0; u < t; u++) mp = max(mp, (int32_t)tm[u]);
-        mprev[threadIdx.x] = mp;
-        mcur[threadIdx.x] = max(mp, (int32_t)tm[t]);
-    }
-    const int16_t *vbase = a.vc + ((size_t)(a.kv_first + slot) * a.max_seq + p0) * hd;
-    for (int i = threadIdx.x; i < tl * hd; i += blockDim.x) {
-        const int p = i / hd, e = i - p * hd;
-        vs[p * kKvStride + e] = (int16_t)sat16((int32_t)vbase[(size_t)p * hd + e] * 16);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * kTile; i += blockDim.x) {
-        const int h = i / kTile, p = i - h * kTile;
-        int32_t pr = 0;
-        if (p < tl) {
-            const int32_t s = a.scores[(hrow + h) * a.max_seq + p0 + p];
-            int32_t d = sat16(s - mcur[h]);
-            d = d < -2048 ? -2048 : (d > 0 ? 0 : d);
-            pr = __ldg(a.ptab + d + 2048);
-        }
-        ps[h][p] = (int16_t)pr;
-    }
-    __syncthreads();
-    if (threadIdx.x < G) {
-        int32_t ts = 0;
-        for (int p = 0; p < tl; p++) ts = add_sat(ts, (int32_t)ps[threadIdx.x][p] * 4);
-        tsum_s[threadIdx.x] = ts;
-        int32_t d = sat16(mprev[threadIdx.x] - mcur[threadIdx.x]);
-        d = d < -2048 ? -2048 : d;
-        const size_t ti = (hrow + threadIdx.x) * a.max_tiles + t;
-        a.tsum[ti] = ts;
-        a.told[ti] = __ldg(a.ptab + d + 2048);
-    }
-    // PV with the raw-payload semantics: payload raw p read as Q8.8 times
-    // V as Q4.12 (saturated) rounded to Q16.16 per product, four banks
-    // (never saturate: |p*v| <= 2^29), x accum(fm(1/64)), -> fm.
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-        const int h = i / hd, e = i - h * hd;
-        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
-        int p = 0;
-        for (; p + 3 < tl; p += 4) {
-            b0 += (int32_t)rnd((int32_t)ps[h][p] * (int32_t)vs[p * kKvStride + e], 4);
-            b1 += (int32_t)rnd((int32_t)ps[h][p + 1] * (int32_t)vs[(p + 1) * kKvStride + e], 4);
-            b2 += (int32_t)rnd((int32_t)ps[h][p + 2] * (int32_t)vs[(p + 2) * kKvStride + e], 4);
-            b3 += (int32_t)rnd((int32_t)ps[h][p + 3] * (int32_t)vs[(p + 3) * kKvStride + e], 4);
-        }
-        if (p < tl) b0 += (int32_t)rnd((int32_t)ps[h][p] * (int32_t)vs[p * kKvStride + e], 4);
-        if (p + 1 < tl) b1 += (int32_t)rnd((int32_t)ps[h][p + 1] * (int32_t)vs[(p + 1) * kKvStride + e], 4);
-        if (p + 2 < tl) b2 += (int32_t)rnd((int32_t)ps[h][p + 2] * (int32_t)vs[(p + 2) * kKvStride + e], 4);
-        int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
-        ts = sat32(rnd((int64_t)ts * 1024, 16));
-        a.tval[((hrow + h) * a.max_tiles + t) * hd + e] = (int16_t)sat16(rnd(ts, 8));
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) ticket_s = atomicAdd(a.tickets + (size_t)r * gridDim.y + slot, 1u);
-    __syncthreads();
-    if (ticket_s != (uint32_t)(ntiles - 1)) return;
-    __threadfence();
-    // sequential Q16.16 recurrence over the tiles, in order
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-        const int h = i / hd, e = i - h * hd;
-        const size_t hb = (hrow + h) * a.max_tiles;
-        int32_t sum = 0, acc = 0;
-        for (int u = 0; u < ntiles; u++) {
-            const int64_t old = (int64_t)__ldcg(a.told + hb + u) * 4;  // Q2.14 -> Q16.16
-            sum = sat32(rnd((int64_t)sum * old, 16) + __ldcg(a.tsum + hb + u));
-            acc = sat32(rnd((int64_t)acc * old, 16));
-            acc = sat32((int64_t)acc + (int64_t)__ldcg(a.tval + (hb + u) * hd + e) * 256);
-        }
-        const int64_t safe = sum < 16 ? 16 : sum;
-        const int64_t quot = ((int64_t)1 << 32) / safe;  // accum(1)/safe, 16 fraction bits
-        const int64_t inv = sat16(rnd(quot, 8));
-        a.out[(size_t)r * a.q_heads * hd + (size_t)(slot * G + h) * hd + e] =
-            (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
-    }
-    if (threadIdx.x == 0) a.tickets[(size_t)r * gridDim.y + slot] = 0;
-}
-
-static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, cudaStream_t s) {
+cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -564,28 +345,14 @@ static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-cudaError_t launch_attn_scores(const AttnArgs &a, int rows, cudaStream_t s) {
-    AttnArgs c = a;
-    void *args[] = {&c};
-    return launch_pdl((const void *)k_attn_scores, dim3(a.max_tiles, a.q_heads / a.group, rows),
-                      dim3(kAttnThreads), args, s);
-}
-
-cudaError_t launch_attn_pv(const AttnArgs &a, int rows, cudaStream_t s) {
-    AttnArgs c = a;
-    void *args[] = {&c};
-    return launch_pdl((const void *)k_attn_pv, dim3(a.max_tiles, a.q_heads / a.group, rows),
-                      dim3(kAttnThreads), args, s);
-}
-
 // --------------------------------------------------------------------------
 // Task 20: final RMSNorm of 1..8 rows (stream_rmsnorm compute_stream.cpp:227-288)
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_rmsnorm(const NormArgs a) {
     __shared__ int64_t red[8];
     __shared__ int32_t inv_s;
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     if (r >= a.step->rows) return;
     const int16_t *x = a.x + (size_t)r * a.n;
@@ -619,8 +386,8 @@ cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s) {
 // tensor parallel: round the all-reduced exact sums and add the residual
 // --------------------------------------------------------------------------
 __global__ void k_round_resid(const ResidArgs a) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int rows = a.step->rows;
     const int total = rows * a.n;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x)

@@ -47,25 +47,22 @@ struct ProjArgs {
     int max_seq;
 };
 
+constexpr int kCluster = 8;         // CTAs per (row, query head) attention cluster
+constexpr int kMaxTilesPerCta = 5;  // bounds the cluster's shared memory: max_seq <= 2560
+
 struct AttnArgs {
     const int16_t *q;    // [8][q_heads*hd] post-RoPE queries of this rank
     const int16_t *kc;   // layer K cache [kv_heads][max_seq][hd]
     const int16_t *vc;
-    int16_t *scores;     // [8][q_heads][max_seq]
-    int16_t *tmax;       // [8][q_heads][max_tiles]
-    int16_t *tval;       // [8][q_heads][max_tiles][hd]
-    int32_t *tsum;       // [8][q_heads][max_tiles]
-    int16_t *told;       // [8][q_heads][max_tiles]
-    uint32_t *tickets;   // [8][kv_groups]
     int16_t *out;        // [8][q_heads*hd]
     const int16_t *ptab; // softmax exp table (2049 entries)
     const Step *step;
     int q_heads;         // query heads on this rank
-    int group;           // query heads per KV head
-    int kv_first;        // first KV head used by this rank
+    int first_head;      // global index of local head 0
+    int gqa;             // query heads per KV head (model)
     int hd;
     int max_seq;
-    int max_tiles;
+    int tpc_max;         // ceil(ceil(max_seq/64) / kCluster): tiles per CTA at most
     int32_t qk_scale;    // accum(fm(1/sqrt(hd))) raw, Q16.16
 };
 
@@ -89,8 +86,9 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
 
 // Launchers (stream-ordered, programmatic-dependent launch enabled).
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
-cudaError_t launch_attn_scores(const AttnArgs &a, int rows, cudaStream_t s);
-cudaError_t launch_attn_pv(const AttnArgs &a, int rows, cudaStream_t s);
+cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s);
+cudaError_t attn_configure(int max_smem_bytes);
+size_t attn_smem_bytes(int tpc, int hd);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 size_t proj_smem_bytes(int rows_tmpl, int K);

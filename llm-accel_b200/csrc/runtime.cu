@@ -60,7 +60,7 @@ struct llmx_ctx {
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;
     // geometry of this rank
-    int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, max_tiles = 0;
+    int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, tpc_max = 0;
     // weights: per layer [QKV | O | GU | D] words
     size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
     uint32_t *wbuf = nullptr;
@@ -71,9 +71,6 @@ struct llmx_ctx {
     int16_t *hid[2] = {nullptr, nullptr};
     int16_t *q = nullptr, *att = nullptr, *act = nullptr;
     int64_t *partial = nullptr;
-    int16_t *scores = nullptr, *tmax = nullptr, *tval = nullptr, *told = nullptr;
-    int32_t *tsum = nullptr;
-    uint32_t *tickets = nullptr;
     Step *step = nullptr;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
@@ -155,21 +152,15 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.q = c->q;
     t.kc = kc_layer(c, layer);
     t.vc = vc_layer(c, layer);
-    t.scores = c->scores;
-    t.tmax = c->tmax;
-    t.tval = c->tval;
-    t.tsum = c->tsum;
-    t.told = c->told;
-    t.tickets = c->tickets;
     t.out = c->att;
     t.ptab = c->ptab;
     t.step = c->step;
     t.q_heads = c->hq;
-    t.group = std::min(c->G, c->hq);
-    t.kv_first = c->h0 / c->G;
+    t.first_head = c->h0;
+    t.gqa = c->G;
     t.hd = c->hd;
     t.max_seq = c->s.max_seq;
-    t.max_tiles = c->max_tiles;
+    t.tpc_max = c->tpc_max;
     t.qk_scale = c->qk_scale;
     return t;
 }
@@ -230,12 +221,10 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         const ProjArgs a = qkv_args(c, layer, in);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
-        const AttnArgs t = attn_args(c, layer);
-        CK(launch_attn_scores(t, (int)rows, c->stream));
-        CK(launch_attn_pv(t, (int)rows, c->stream));
+        CK(launch_attn(attn_args(c, layer), (int)rows, c->stream));
         const ProjArgs o = o_args(c, layer, out, in);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
-        c->launches += 4;
+        c->launches += 3;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
         return LLMX_OK;
     }
@@ -361,7 +350,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->Hq = hq * hd;
     c->Il = s.inter / tp_size;
     c->c0 = tp_rank * c->Il;
-    c->max_tiles = (s.max_seq + kTile - 1) / kTile;
+    c->tpc_max = ((s.max_seq + kTile - 1) / kTile + kCluster - 1) / kCluster;
     c->layer_loaded.assign(s.layers, false);
     auto bail = [&](int code) {
         release(c);
@@ -377,6 +366,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
     e = proj_configure(200 * 1024);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
+    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd));
+    if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
 
     const size_t H = s.hidden;
     c->w_qkv = (size_t)(c->Hq + 2 * c->KV) * H / 2;
@@ -385,7 +376,6 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->w_d = H * (size_t)c->Il / 2;
     c->layer_words = c->w_qkv + c->w_o + c->w_gu + c->w_d;
     const size_t kv_elems = (size_t)s.layers * s.kv_heads * s.max_seq * hd;
-    const size_t mt = c->max_tiles;
     if ((rc = dalloc(c, &c->wbuf, c->layer_words * s.layers)) ||
         (rc = dalloc(c, &c->staging, layer_elems(s))) ||
         (rc = dalloc(c, &c->slot_qkv, c->Hq + 2 * c->KV)) || (rc = dalloc(c, &c->slot_o, H)) ||
@@ -397,12 +387,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->att, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->act, kMaxRows * (size_t)c->Il)) || (rc = dalloc(c, &c->partial, kMaxRows * H)) ||
-        (rc = dalloc(c, &c->scores, kMaxRows * (size_t)hq * s.max_seq)) ||
-        (rc = dalloc(c, &c->tmax, kMaxRows * (size_t)hq * mt)) ||
-        (rc = dalloc(c, &c->tval, kMaxRows * (size_t)hq * mt * hd)) ||
-        (rc = dalloc(c, &c->tsum, kMaxRows * (size_t)hq * mt)) ||
-        (rc = dalloc(c, &c->told, kMaxRows * (size_t)hq * mt)) ||
-        (rc = dalloc(c, &c->tickets, kMaxRows * (size_t)s.kv_heads)) || (rc = dalloc(c, &c->step, 1)))
+        (rc = dalloc(c, &c->step, 1)))
         return bail(rc);
 
     // slot -> dense row tables of the pair-interleaved layout
@@ -661,8 +646,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
             const ProjArgs a = qkv_args(c, layer, in);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
-        case LLMX_KERNEL_ATTN_SCORES: return launch_attn_scores(attn_args(c, layer), (int)rows, c->stream);
-        case LLMX_KERNEL_ATTN_PV: return launch_attn_pv(attn_args(c, layer), (int)rows, c->stream);
+        case LLMX_KERNEL_ATTN: return launch_attn(attn_args(c, layer), (int)rows, c->stream);
         case LLMX_KERNEL_O: {
             const ProjArgs o = o_args(c, layer, out, in);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);

@@ -90,6 +90,8 @@ int llmx_shape_validate(const llmx_shape *s) {
     // of 8 and <= 128.
     if (hd % 8 || hd > 128 || s->heads / s->kv_heads > 8) return LLMX_ERR_UNSUPPORTED;
     if (s->hidden % 8 || s->inter % 8) return LLMX_ERR_UNSUPPORTED;
+    // one attention cluster (8 CTAs x 5 tiles of 64) covers the context
+    if (s->max_seq > 8 * 5 * 64) return LLMX_ERR_UNSUPPORTED;
     return LLMX_OK;
 }
 

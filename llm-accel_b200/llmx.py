@@ -26,7 +26,7 @@ BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 
 ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED = range(100, 108)
 OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
 MAX_ROWS = 8
-KERNEL_QKV, KERNEL_ATTN_SCORES, KERNEL_ATTN_PV, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(7)
+KERNEL_QKV, KERNEL_ATTN, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(6)
 
 
 class LlmxError(RuntimeError):

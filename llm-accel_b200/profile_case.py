@@ -20,7 +20,7 @@ import numpy as np
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 import llmx  # noqa: E402
 
-NAMES = ["qkv", "attn_scores", "attn_pv", "o_proj", "gate_up", "down", "final_norm"]
+NAMES = ["qkv", "attention", "o_proj", "gate_up", "down", "final_norm"]
 
 
 def main():
