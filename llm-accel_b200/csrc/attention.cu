@@ -13,16 +13,19 @@
 //
 // One thread-block cluster of kCluster CTAs handles one (row, query head).
 // CTA c owns the contiguous tiles [c*tpc, (c+1)*tpc):
-//   1. K and V rows of its tiles land in shared memory (cp.async, issued
-//      together); QK scores of its positions and its tile maxima;
-//   2. cluster barrier; running maxima from all owners' tile maxima (DSMEM);
-//      Q2.14 probabilities, tile sums, rescale factors and the raw-payload PV
-//      tile values of its tiles;
-//   3. cluster barrier; the (sum, acc) recurrence in tile order, each CTA
-//      finalising hd/kCluster output elements from the owners' tile values;
-//   4. cluster barrier, so no CTA leaves while its shared memory is read.
-// All waits are hardware cluster barriers: no flags, no spin loops, and no
-// global scratch memory.
+//   1. K rows of its tiles land in shared memory (cp.async); QK scores of its
+//      positions; the buffer is refilled with the V rows while each owned
+//      tile's maximum is stored into every CTA's shared memory (DSMEM push);
+//   2. cluster barrier; running maxima (prefix max of the pushed maxima),
+//      Q2.14 probabilities, tile sums and rescale factors (pushed to every
+//      CTA) and the raw-payload PV tile values, each pushed to the CTA that
+//      finalises that output element;
+//   3. cluster barrier; the (sum, acc) recurrence in tile order on local
+//      shared memory, each CTA finalising hd/kCluster output elements.
+// All remote accesses are stores issued before a barrier, so after each
+// barrier a CTA reads only its own shared memory, and no CTA needs to wait for
+// the others before it exits.  All waits are hardware cluster barriers: no
+// flags, no spin loops, and no global scratch memory.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -46,40 +49,48 @@ static __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
-struct AttnSmem {   // carved out of dynamic shared memory
-    int16_t *k, *v; // [tpc*64][kKvStride] raw Q8.8 rows of the owned tiles
-    int16_t *q;     // [hd]
-    int16_t *sc;    // [tpc*64] scores, then Q2.14 probabilities
-    int16_t *tval;  // [tpc][hd] owned PV tile values (Q8.8)
-    int32_t *tmax;  // [tpc] owned tile maxima
-    int32_t *tsum;  // [tpc] owned tile sums (Q16.16)
-    int32_t *told;  // [tpc] owned rescale factors (Q2.14)
-    int32_t *mall;  // [kCluster*tpc] running max after every tile
-    int32_t *gsum;  // [kCluster*tpc] gathered tile sums
-    int32_t *gold;  // [kCluster*tpc] gathered rescale factors
+constexpr int kMaxTiles = kCluster * kMaxTilesPerCta;
+
+struct AttnSmem {      // carved out of dynamic shared memory
+    int16_t *kv;       // [tpc*64][kKvStride] raw Q8.8 K rows, then V rows, of the owned tiles
+    int16_t *ptab;     // [2049] softmax exp table
+    int16_t *q;        // [hd]
+    int16_t *sc;       // [tpc*64] scores, then Q2.14 probabilities
+    int16_t *tvr;      // [kMaxTiles][hd/kCluster] tile values of the elements this CTA finalises
+    int32_t *mloc;     // [kMaxTiles] every tile's maximum (pushed by the owners)
+    int32_t *gsum;     // [kMaxTiles] every tile's sum (pushed)
+    int32_t *gold;     // [kMaxTiles] every tile's rescale factor (pushed)
+    int32_t *tsum;     // [tpc] owned tile sums (local accumulation)
 };
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, size_t off[10]) {
+static __host__ __device__ size_t attn_layout(int tpc, int hd, size_t off[9]) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
-    off[0] = b; b = align16(b + rows * kKvStride * 2);           // k
-    off[1] = b; b = align16(b + rows * kKvStride * 2);           // v
-    off[2] = b; b = align16(b + (size_t)kMaxHd * 2);             // q
-    off[3] = b; b = align16(b + rows * 2);                       // sc
-    off[4] = b; b = align16(b + (size_t)tpc * hd * 2);           // tval
-    off[5] = b; b = align16(b + (size_t)tpc * 4);                // tmax
-    off[6] = b; b = align16(b + (size_t)tpc * 4);                // tsum
-    off[7] = b; b = align16(b + (size_t)tpc * 4);                // told
-    off[8] = b; b = align16(b + (size_t)kCluster * tpc * 4);     // mall
-    off[9] = b; b = align16(b + (size_t)kCluster * tpc * 4 * 2); // gsum, gold
+    off[0] = b; b = align16(b + rows * kKvStride * 2);                       // kv
+    off[1] = b; b = align16(b + 2049 * 2);                                   // ptab
+    off[2] = b; b = align16(b + (size_t)kMaxHd * 2);                         // q
+    off[3] = b; b = align16(b + rows * 2);                                   // sc
+    off[4] = b; b = align16(b + (size_t)kMaxTiles * (kMaxHd / kCluster) * 2); // tvr
+    off[5] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // mloc
+    off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
+    off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
+    off[8] = b; b = align16(b + (size_t)tpc * 4);                            // tsum
+    (void)hd;
     return b;
 }
 
 size_t attn_smem_bytes(int tpc, int hd) {
-    size_t off[10];
+    size_t off[9];
     return attn_layout(tpc, hd, off);
+}
+
+// floor(2^32 / s) for 16 <= s < 2^31 (the quotient of accum(1) / safe_sum,
+// host:3727-3730: (1.0 << 16) / s with 16 fraction bits, truncated)
+static __device__ __forceinline__ uint32_t recip_q16(int32_t s) {
+    const uint32_t u = (uint32_t)s;
+    return 0xffffffffu / u + ((u & (u - 1)) == 0 ? 1u : 0u);
 }
 
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
@@ -88,26 +99,26 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int c = (int)cluster.block_rank();
     const int lh = blockIdx.x / kCluster;  // local query head
     const int r = blockIdx.y;
-    const int hd = a.hd, vpr = hd >> 3;
-    size_t off[10];
+    const int hd = a.hd, vpr = hd >> 3, epc = hd / kCluster;  // elements finalised per CTA
+    size_t off[9];
     attn_layout(a.tpc_max, hd, off);
     AttnSmem m;
-    m.k = reinterpret_cast<int16_t *>(raw + off[0]);
-    m.v = reinterpret_cast<int16_t *>(raw + off[1]);
+    m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
+    m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
     m.q = reinterpret_cast<int16_t *>(raw + off[2]);
     m.sc = reinterpret_cast<int16_t *>(raw + off[3]);
-    m.tval = reinterpret_cast<int16_t *>(raw + off[4]);
-    m.tmax = reinterpret_cast<int32_t *>(raw + off[5]);
-    m.tsum = reinterpret_cast<int32_t *>(raw + off[6]);
-    m.told = reinterpret_cast<int32_t *>(raw + off[7]);
-    m.mall = reinterpret_cast<int32_t *>(raw + off[8]);
-    m.gsum = reinterpret_cast<int32_t *>(raw + off[9]);
-    m.gold = m.gsum + kCluster * a.tpc_max;
+    m.tvr = reinterpret_cast<int16_t *>(raw + off[4]);
+    m.mloc = reinterpret_cast<int32_t *>(raw + off[5]);
+    m.gsum = reinterpret_cast<int32_t *>(raw + off[6]);
+    m.gold = reinterpret_cast<int32_t *>(raw + off[7]);
+    m.tsum = reinterpret_cast<int32_t *>(raw + off[8]);
 
+    // the exp table does not depend on the producer kernel
+    for (int i = threadIdx.x; i < 2049; i += blockDim.x) m.ptab[i] = a.ptab[i];
     pdl_wait();
     pdl_trigger();
     const Step st = *a.step;
-    // every CTA of the cluster reaches every barrier, also when it owns nothing
+    // every CTA of the cluster reaches both cluster barriers, also when it owns nothing
     const bool row_ok = r < st.rows;
     const int ctx = st.position + r + 1;
     const int ntiles = row_ok ? (ctx + kTile - 1) / kTile : 0;
@@ -117,29 +128,25 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int p_begin = t_begin * kTile;
     const int npos = nown > 0 ? min(t_end * kTile, ctx) - p_begin : 0;
     const int kvh = (a.first_head + lh) / a.gqa;
+    const int16_t *kb = a.kc + ((size_t)kvh * a.max_seq + p_begin) * hd;
+    const int16_t *vb = a.vc + ((size_t)kvh * a.max_seq + p_begin) * hd;
 
+    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
+        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
+        cp_async16(m.kv + pp * kKvStride + cc, kb + (size_t)pp * hd + cc);
+    }
     if (npos > 0) {
-        const int16_t *kb = a.kc + ((size_t)kvh * a.max_seq + p_begin) * hd;
-        const int16_t *vb = a.vc + ((size_t)kvh * a.max_seq + p_begin) * hd;
-        for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-            const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-            cp_async16(m.k + pp * kKvStride + cc, kb + (size_t)pp * hd + cc);
-            cp_async16(m.v + pp * kKvStride + cc, vb + (size_t)pp * hd + cc);
-        }
         const uint4 *qsrc = reinterpret_cast<const uint4 *>(a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd);
         for (int i = threadIdx.x; i < vpr; i += blockDim.x) reinterpret_cast<uint4 *>(m.q)[i] = qsrc[i];
-        for (int i = threadIdx.x; i < nown; i += blockDim.x) {
-            m.tmax[i] = -32768;
-            m.tsum[i] = 0;
-        }
-        cp_async_wait_all();
     }
+    for (int i = threadIdx.x; i < nown; i += blockDim.x) m.tsum[i] = 0;
+    cp_async_wait_all();
     __syncthreads();
 
-    // ---- 1. scores and owned tile maxima ---------------------------------
+    // ---- 1. scores; owned tile maxima pushed to every CTA of the cluster ----
     for (int pp = threadIdx.x; pp < npos; pp += blockDim.x) {
         const uint4 *qv = reinterpret_cast<const uint4 *>(m.q);
-        const uint4 *kv = reinterpret_cast<const uint4 *>(m.k + pp * kKvStride);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
         int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;  // banks k mod 4, saturating, in k order
         for (int e8 = 0; e8 < vpr; e8++) {
             const uint4 q = qv[e8], k = kv[e8];
@@ -156,91 +163,90 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));  // x accum(fm(1/sqrt(d)))
         const int32_t sc = sat16(rnd(tot, 8));
         m.sc[pp] = (int16_t)sc;
-        atomicMax(m.tmax + pp / kTile, sc);
+    }
+    __syncthreads();  // K consumed: the buffer now receives V (overlaps the exchange below)
+    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
+        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
+        cp_async16(m.kv + pp * kKvStride + cc, vb + (size_t)pp * hd + cc);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    {   // tile maxima: one warp per owned tile
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int tl = warp; tl < nown; tl += blockDim.x >> 5) {
+            const int pe = min(kTile, npos - tl * kTile);
+            int32_t mx = -32768;
+            for (int j = lane; j < pe; j += 32) mx = max(mx, (int32_t)m.sc[tl * kTile + j]);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane < kCluster) *cluster.map_shared_rank(m.mloc + t_begin + tl, lane) = mx;
+        }
     }
     cluster.sync();
 
-    // ---- 2. running maxima, probabilities, tile sums, rescale, PV --------
-    if (threadIdx.x == 0 && nown > 0) {
-        int32_t run = -32768;  // m_{-1} = fm(-128)
-        for (int t = 0; t < t_end; t++) {
-            const int owner = t / tpc;
-            run = max(run, *cluster.map_shared_rank(m.tmax + (t - owner * tpc), owner));
-            m.mall[t] = run;
-        }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < nown; i += blockDim.x) {
-        const int t = t_begin + i;
-        const int32_t mprev = t > 0 ? m.mall[t - 1] : -32768;
-        int32_t d = sat16(mprev - m.mall[t]);
-        d = d < -2048 ? -2048 : d;
-        m.told[i] = __ldg(a.ptab + d + 2048);
-    }
+    // ---- 2. running maxima, probabilities, tile sums, rescale, PV ----------
+    // running max after tile t = prefix max of tile maxima, m_{-1} = fm(-128)
     for (int pp = threadIdx.x; pp < npos; pp += blockDim.x) {
-        int32_t d = sat16((int32_t)m.sc[pp] - m.mall[t_begin + pp / kTile]);
+        const int t = t_begin + pp / kTile;
+        int32_t mt = -32768;
+        for (int u = 0; u <= t; u++) mt = max(mt, m.mloc[u]);
+        int32_t d = sat16((int32_t)m.sc[pp] - mt);
         d = d < -2048 ? -2048 : (d > 0 ? 0 : d);
-        const int32_t pr = __ldg(a.ptab + d + 2048);
+        const int32_t pr = m.ptab[d + 2048];
         m.sc[pp] = (int16_t)pr;
         atomicAdd(m.tsum + pp / kTile, pr * 4);  // Q2.14 -> Q16.16; <= 64 * 2^16, never saturates
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
+    for (int i = threadIdx.x; i < nown; i += blockDim.x) {  // tile sum + rescale factor -> every CTA
+        const int t = t_begin + i;
+        int32_t mprev = -32768, mt = -32768;
+        for (int u = 0; u < t; u++) mprev = max(mprev, m.mloc[u]);
+        mt = max(mprev, m.mloc[t]);
+        int32_t d = sat16(mprev - mt);
+        d = d < -2048 ? -2048 : d;
+        const int32_t old = m.ptab[d + 2048];
+        for (int k = 0; k < kCluster; k++) {
+            *cluster.map_shared_rank(m.gsum + t, k) = m.tsum[i];
+            *cluster.map_shared_rank(m.gold + t, k) = old;
+        }
+    }
     // raw payload p (read as Q8.8) x V (Q4.12, saturated), rounded per product,
     // four banks in position order (|p*v| <= 2^29: banks never saturate),
-    // x accum(fm(1/64)), -> fm
+    // x accum(fm(1/64)), -> fm; pushed to the CTA that finalises element e
     for (int i = threadIdx.x; i < nown * hd; i += blockDim.x) {
         const int tli = i / hd, e = i - tli * hd;
         const int pb = tli * kTile, pe = min(pb + kTile, npos);
         int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
         int pp = pb;
         for (; pp + 3 < pe; pp += 4) {
-            b0 += qk_prod(m.sc[pp], q412(m.v[pp * kKvStride + e]));
-            b1 += qk_prod(m.sc[pp + 1], q412(m.v[(pp + 1) * kKvStride + e]));
-            b2 += qk_prod(m.sc[pp + 2], q412(m.v[(pp + 2) * kKvStride + e]));
-            b3 += qk_prod(m.sc[pp + 3], q412(m.v[(pp + 3) * kKvStride + e]));
+            b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
+            b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+            b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+            b3 += qk_prod(m.sc[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
         }
-        if (pp < pe) b0 += qk_prod(m.sc[pp], q412(m.v[pp * kKvStride + e]));
-        if (pp + 1 < pe) b1 += qk_prod(m.sc[pp + 1], q412(m.v[(pp + 1) * kKvStride + e]));
-        if (pp + 2 < pe) b2 += qk_prod(m.sc[pp + 2], q412(m.v[(pp + 2) * kKvStride + e]));
+        if (pp < pe) b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
+        if (pp + 1 < pe) b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+        if (pp + 2 < pe) b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
         int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
         ts = sat32(rnd((int64_t)ts * 1024, 16));
-        m.tval[tli * hd + e] = (int16_t)sat16(rnd(ts, 8));
+        const int16_t tv = (int16_t)sat16(rnd(ts, 8));
+        *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / kCluster, e % kCluster) = tv;
     }
     cluster.sync();
 
-    // ---- 3. in-order Q16.16 recurrence ------------------------------------
-    for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
-        const int owner = i / tpc;
-        m.gsum[i] = *cluster.map_shared_rank(m.tsum + (i - owner * tpc), owner);
-        m.gold[i] = *cluster.map_shared_rank(m.told + (i - owner * tpc), owner);
-    }
-    __syncthreads();
-    for (int e = c + kCluster * (int)threadIdx.x; ntiles > 0 && e < hd; e += kCluster * blockDim.x) {
+    // ---- 3. in-order Q16.16 recurrence on local shared memory ---------------
+    for (int j = threadIdx.x; ntiles > 0 && j < epc; j += blockDim.x) {
+        const int e = j * kCluster + c;
         int32_t sum = 0, acc = 0;
-        for (int u0 = 0; u0 < ntiles; u0 += 8) {
-            int32_t tv[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {  // fetch 8 tiles' values before using them
-                const int u = u0 + j, owner = u / tpc;
-                tv[j] = u < ntiles ? *cluster.map_shared_rank(m.tval + (u - owner * tpc) * hd + e, owner) : 0;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int u = u0 + j;
-                if (u < ntiles) {
-                    const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
-                    sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[u]);
-                    acc = sat32(rnd((int64_t)acc * o, 16));
-                    acc = sat32((int64_t)acc + (int64_t)tv[j] * 256);
-                }
-            }
+        for (int u = 0; u < ntiles; u++) {
+            const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
+            sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[u]);
+            acc = sat32(rnd((int64_t)acc * o, 16));
+            acc = sat32((int64_t)acc + (int64_t)m.tvr[u * epc + j] * 256);
         }
-        const int64_t safe = sum < 16 ? 16 : sum;
-        const int64_t quot = ((int64_t)1 << 32) / safe;  // accum(1) / safe: 16 fraction bits, truncated
-        const int64_t inv = sat16(rnd(quot, 8));
-        a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = (int16_t)sat16(rnd(acc * inv * 256, 24));
+        const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
+        a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
     }
-    cluster.sync();
 }
 
 cudaError_t attn_configure(int max_smem_bytes) {
