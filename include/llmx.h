@@ -42,6 +42,7 @@ extern "C" {
 #define LLMX_ERR_NOMEM 105    /* device or host allocation failed */
 #define LLMX_ERR_IO 106       /* checkpoint file missing or wrong size */
 #define LLMX_ERR_UNSUPPORTED 107
+#define LLMX_ERR_TIMEOUT 108     /* a kernel's bounded wait expired (device error flag) */
 
 /* ---- coarse operators: operator_kind_t host:69-91 / cc8_operator_t
  *      include/control_cache_8x64.hpp:252-277 (only the resident tasks) ---- */

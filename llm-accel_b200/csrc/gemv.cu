@@ -1,0 +1,419 @@
+// Weight-streaming projection kernel of the resident layer path.
+//
+// Reference arithmetic: the 8x64 fused MAC engine accumulates raw int16 x int16
+// products exactly and rounds twice at the end (Q28.20 -> Q16.16 -> Q8.8):
+// kernel/mm_stream_8x64_fused_mac.cpp:11-22,89-96,138-205 and
+// kernel/compute_core_8x64_unified.cpp:10-39 (golden_projection host:3105-3142).
+//
+// B200 mapping.  One persistent CTA per SM owns a contiguous slice of the
+// weight matrix (whole "units": one output row, or a RoPE / gate-up pair of
+// rows).  A producer thread streams the slice through a shared-memory ring
+// with 1-D bulk copies (cp.async.bulk, completion on an mbarrier); eight
+// consumer warps take units round-robin, read weights and activations with
+// 128-bit shared loads and form exact products with the dp2a pipe (weights
+// pre-split into unsigned low / signed high bytes, activations packed int16
+// pairs), so every MAC is exact and the reduction order is free.  The producer
+// starts streaming before the programmatic-dependent-launch wait: weights do
+// not depend on the previous kernel, so HBM keeps streaming across kernel
+// boundaries.  Each ring wait is bounded; on expiry the kernel records an
+// error code in device memory, drains its own copies and returns.
+//
+// Epilogues fuse what follows the projection in the controller schedule:
+// RoPE + KV-cache append (Q/K/V), residual add (O, Down), SiLU(gate) x up
+// (Gate/Up), or exact int64 partial sums for the tensor-parallel all-reduce.
+#include <cuda_runtime.h>
+
+#include "device_util.cuh"
+#include "fixed.cuh"
+#include "kernels.cuh"
+
+namespace llmx {
+
+constexpr int kConsumers = 8;                       // consumer warps
+constexpr int kGemvThreads = (kConsumers + 1) * 32; // + one producer warp
+constexpr int kRingBytes = 96 * 1024;               // target weight bytes in flight per SM
+constexpr int kMaxStages = 32;
+constexpr uint32_t kSpinLimit = 1u << 26;           // bounded mbarrier waits (seconds of polling)
+
+// ---- mbarrier / bulk-copy primitives ---------------------------------------
+static __device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+static __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+static __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+static __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+static __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when the limit expired (the caller records an error).
+static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+static __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+static __device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+}
+
+// golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
+// then x up with one rounding (stream_silu_mul :123-164).
+static __device__ __forceinline__ int32_t silu_mul(int32_t g, int32_t u, const int16_t *__restrict__ etab) {
+    int32_t s;
+    if (g >= 0) {
+        const int32_t e = __ldg(etab + (g > 2048 ? 0 : 2048 - g));
+        const int32_t r = recip_q88(sat16(256 + e));
+        s = sat16(rnd((int64_t)g * r, 8));
+    } else {
+        const int32_t e = __ldg(etab + (g < -2048 ? 0 : g + 2048));
+        const int32_t r = recip_q88(sat16(256 + e));
+        s = sat16(rnd((int64_t)g * e * r, 16));
+    }
+    return sat16(rnd((int64_t)s * u, 8));
+}
+
+// Halving ("transpose") warp reduction of N int64 values: afterwards lane L
+// holds the warp total of value index idx(L); lanes that differ only in the
+// bits below 32/N hold the same index.  N <= 16.
+template <int N>
+static __device__ __forceinline__ int64_t warp_reduce_n(int64_t (&v)[N], int lane, int &idx) {
+    idx = 0;
+#pragma unroll
+    for (int n = N, o = 16; n > 1; n >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) {
+            const int64_t send = up ? v[i] : v[i + n / 2];
+            const int64_t keep = up ? v[i + n / 2] : v[i];
+            v[i] = keep + shfl_xor64(send, o);
+        }
+        if (up) idx += n / 2;
+    }
+    int64_t t = v[0];
+#pragma unroll
+    for (int o = 16 / N; o >= 1; o >>= 1) t += shfl_xor64(t, o);
+    return t;
+}
+
+// Activation prologue (consumer warps): rows -> shared memory, RMS-normalised
+// when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
+template <int R>
+static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int tid) {
+    constexpr int T = kConsumers * 32;
+    const int K = a.K, KV8 = K >> 3;
+    __shared__ int32_t inv_rms_s[kMaxRows];
+    if (a.norm != nullptr) {
+        if (a.inv_elems == 0) {
+            // recip(fm(K)) == 0: mean == 0 for every input, inv_rms is a constant
+            if (tid < R) inv_rms_s[tid] = a.inv_rms_const;
+        } else {
+            __shared__ int64_t red[kConsumers][kMaxRows];
+            int64_t part[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) part[r] = 0;
+            for (int i = tid; i < K; i += T) {
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    if (r < rows) {
+                        const int32_t v = a.x[(size_t)r * K + i];
+                        part[r] += (int64_t)v * v;
+                    }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++)
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) part[r] += shfl_xor64(part[r], o);
+            if ((tid & 31) == 0)
+#pragma unroll
+                for (int r = 0; r < R; r++) red[tid >> 5][r] = part[r];
+            consumer_sync();
+            if (tid < R) {
+                int64_t sum = 0;
+                for (int w = 0; w < kConsumers; w++) sum += red[w][tid];
+                // saturating running sum == min(total, INT32_MAX): every term is >= 0
+                inv_rms_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
+            }
+        }
+        consumer_sync();
+        const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
+        const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm);
+        for (int i = tid; i < R * KV8; i += T) {
+            const int r = i / KV8, v = i - r * KV8;
+            uint4 o = make_uint4(0, 0, 0, 0);
+            if (r < rows) {
+                const uint4 xv = x4[(size_t)r * KV8 + v], wv = w4[v];
+                const int64_t inv = inv_rms_s[r];
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                uint32_t ow[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int32_t y0 = sat16(rnd((int64_t)lo16(xw[k]) * inv * lo16(ww[k]), 16));
+                    const int32_t y1 = sat16(rnd((int64_t)hi16(xw[k]) * inv * hi16(ww[k]), 16));
+                    ow[k] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+                }
+                o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
+            reinterpret_cast<uint4 *>(xs)[i] = o;
+        }
+    } else {
+        const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
+        for (int i = tid; i < R * KV8; i += T)
+            reinterpret_cast<uint4 *>(xs)[i] = (i / KV8) < rows ? x4[i] : make_uint4(0, 0, 0, 0);
+    }
+    consumer_sync();
+}
+
+template <int R, int EPI>
+struct GemvTraits {
+    static constexpr int U = (EPI == EPI_QKV || EPI == EPI_SILU) ? 2 : 1;  // rows per unit
+};
+
+// unit -> this CTA's contiguous range [u0, u1)
+static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) {
+    u0 = (int)((int64_t)nunits * blockIdx.x / gridDim.x);
+    u1 = (int)((int64_t)nunits * (blockIdx.x + 1) / gridDim.x);
+}
+
+template <int R, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
+    constexpr int U = GemvTraits<R, EPI>::U;
+    constexpr int N = U * R;  // int64 sums per unit
+    extern __shared__ __align__(128) char smem[];
+    const int K = a.K, KV8 = K >> 3;
+    const int unit_words = U * (K >> 1);
+    const uint32_t unit_bytes = (uint32_t)unit_words * 4;
+    const int S = a.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kMaxStages;
+    char *ring = smem + 2 * kMaxStages * sizeof(uint64_t);
+    int16_t *xs = reinterpret_cast<int16_t *>(ring + (size_t)S * unit_bytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nunits = a.npairs * 2 / U;
+    int u0, u1;
+    unit_range(nunits, u0, u1);
+    const int nloc = u1 - u0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kConsumers) {  // ---------------- producer warp -------------
+        if (lane == 0) {
+            const char *src = reinterpret_cast<const char *>(a.w) + (size_t)u0 * unit_bytes;
+            bool ok = true;
+            for (int j = 0; j < nloc; j++) {
+                const int s = j % S;
+                if (j >= S && !mbar_wait(empty + s, ((j / S) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(full + s, unit_bytes);
+                bulk_g2s(ring + (size_t)s * unit_bytes, src + (size_t)j * unit_bytes, unit_bytes, full + s);
+                if (j == S - 1) pdl_wait();  // ring primed before waiting on the producer kernel
+            }
+            if (nloc < S) pdl_wait();
+            if (!ok) {
+                atomicExch(a.error, 1);
+                // drain: wait (bounded) for every copy this thread issued to land
+                for (int s = 0; s < S && s < nloc; s++) (void)mbar_wait(full + s, ((nloc - 1 - s) / S) & 1);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------------------------------
+    const int tid = threadIdx.x;  // 0 .. 255
+    pdl_wait();
+    pdl_trigger();
+    const Step st = *a.step;
+    const int rows = st.rows;
+    stage_rows<R>(a, xs, rows, tid);
+    const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
+
+    for (int j = warp; j < nloc; j += kConsumers) {
+        const int s = j % S;
+        if (!__all_sync(0xffffffffu, mbar_wait(full + s, (j / S) & 1))) {  // warp-uniform decision
+            if (lane == 0) atomicExch(a.error, 2);
+            break;
+        }
+        const uint4 *wv = reinterpret_cast<const uint4 *>(ring + (size_t)s * unit_bytes);
+        int64_t acc[N];
+#pragma unroll
+        for (int i = 0; i < N; i++) acc[i] = 0;
+        for (int v0 = 0; v0 < KV8; v0 += 16 * 32) {  // int32 partials flushed every 16 vectors per lane
+            int lo[N], hi[N];
+#pragma unroll
+            for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
+#pragma unroll 4
+            for (int k = 0; k < 16; k++) {
+                const int v = v0 + k * 32 + lane;
+                if (v < KV8) {
+                    uint4 w[U];
+#pragma unroll
+                    for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        const uint4 x = xs4[r * KV8 + v];
+#pragma unroll
+                        for (int u = 0; u < U; u++) {
+                            const int i = r * U + u;
+                            lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
+                            hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
+                            lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
+                            hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
+                            lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
+                            hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
+                            lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
+                            hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
+                        }
+                    }
+                }
+            }
+            // |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29
+#pragma unroll
+            for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);  // stage free for the producer
+
+        int idx;
+        const int64_t tot = warp_reduce_n<N>(acc, lane, idx);
+        const int unit = u0 + j;
+        if (U == 2) {
+            constexpr int kPartnerBit = 32 / N;
+            const int64_t other = __shfl_sync(0xffffffffu, tot, lane | kPartnerBit);
+            const int r = idx >> 1;
+            if ((lane & (kPartnerBit - 1)) != 0 || (idx & 1) != 0 || r >= rows) continue;
+            const int32_t y0 = round_mac(tot), y1 = round_mac(other);
+            if (EPI == EPI_SILU) {
+                a.out[(size_t)r * a.out_stride + unit] = (int16_t)silu_mul(y0, y1, a.etab);
+            } else {  // EPI_QKV: unit = pair (i, i + hd/2) of a head
+                const int half = a.hd >> 1;
+                const int pos = st.position + r;
+                int pp = unit;
+                if (pp < a.q_pairs + a.kv_pairs) {
+                    // RoPE rotate_fix16_pair_with_quantized_rope host:4765-4788
+                    const bool isq = pp < a.q_pairs;
+                    if (!isq) pp -= a.q_pairs;
+                    const int head = pp / half, i = pp - head * half;
+                    const int64_t cs = a.rope[(size_t)pos * a.hd + i];
+                    const int64_t sn = a.rope[(size_t)pos * a.hd + half + i];
+                    const int16_t z0 = (int16_t)sat16(rnd((int64_t)y0 * cs - (int64_t)y1 * sn, 8));
+                    const int16_t z1 = (int16_t)sat16(rnd((int64_t)y1 * cs + (int64_t)y0 * sn, 8));
+                    int16_t *dst = isq ? a.out + (size_t)r * a.out_stride + (size_t)head * a.hd
+                                       : a.kc + ((size_t)head * a.max_seq + pos) * a.hd;
+                    dst[i] = z0;
+                    dst[i + half] = z1;
+                } else {
+                    pp -= a.q_pairs + a.kv_pairs;
+                    const int head = pp / half, i = pp - head * half;
+                    int16_t *dst = a.vc + ((size_t)head * a.max_seq + pos) * a.hd;
+                    dst[i] = (int16_t)y0;
+                    dst[i + half] = (int16_t)y1;
+                }
+            }
+        } else {
+            const int r = idx;
+            if ((lane & (32 / N - 1)) != 0 || r >= rows) continue;
+            if (EPI == EPI_PARTIAL) {
+                a.partial[(size_t)r * a.out_stride + unit] = tot;
+            } else {  // EPI_RESID
+                const size_t o = (size_t)r * a.out_stride + unit;
+                a.out[o] = (int16_t)sat16((int32_t)a.resid[o] + round_mac(tot));
+            }
+        }
+    }
+}
+
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages) {
+    const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
+    return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * U * K * 2 + (size_t)rows_tmpl * K * 2;
+}
+
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem) {
+    const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
+    const size_t unit = (size_t)U * K * 2;
+    int s = (int)(kRingBytes / unit);
+    if (s > kMaxStages) s = kMaxStages;
+    if (s < 2) s = 2;
+    while (s > 2 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;
+    return s;
+}
+
+template <int R, int EPI>
+static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
+    ProjArgs c = a;
+    void *args[] = {&c};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI>, args);
+}
+
+template <int EPI>
+static cudaError_t launch_gemv_r(const ProjArgs &a, int rows_tmpl, int grid, cudaStream_t s) {
+    switch (rows_tmpl) {
+    case 1: return launch_gemv_t<1, EPI>(a, grid, s);
+    case 2: return launch_gemv_t<2, EPI>(a, grid, s);
+    case 4: return launch_gemv_t<4, EPI>(a, grid, s);
+    default: return launch_gemv_t<8, EPI>(a, grid, s);
+    }
+}
+
+cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s) {
+    switch (epi) {
+    case EPI_QKV: return launch_gemv_r<EPI_QKV>(a, rows_tmpl, grid, s);
+    case EPI_RESID: return launch_gemv_r<EPI_RESID>(a, rows_tmpl, grid, s);
+    case EPI_SILU: return launch_gemv_r<EPI_SILU>(a, rows_tmpl, grid, s);
+    default: return launch_gemv_r<EPI_PARTIAL>(a, rows_tmpl, grid, s);
+    }
+}
+
+template <int EPI>
+static cudaError_t configure_epi(int bytes) {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_gemv<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemv<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_gemv<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    return cudaFuncSetAttribute(k_gemv<8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+cudaError_t proj_configure(int max_smem_bytes) {
+    cudaError_t e;
+    if ((e = configure_epi<EPI_QKV>(max_smem_bytes))) return e;
+    if ((e = configure_epi<EPI_RESID>(max_smem_bytes))) return e;
+    if ((e = configure_epi<EPI_SILU>(max_smem_bytes))) return e;
+    return configure_epi<EPI_PARTIAL>(max_smem_bytes);
+}
+
+}  // namespace llmx

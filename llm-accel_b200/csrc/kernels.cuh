@@ -7,7 +7,6 @@ namespace llmx {
 
 constexpr int kTile = 64;     // online-softmax tile: include/control_cache_8x64.hpp:72
 constexpr int kMaxRows = 8;   // kMaxTokensPerLaunch host:38
-constexpr int kWarps = 8;     // warps per CTA of the projection kernels
 
 // Position/row count of the running task, read by every kernel from device
 // memory so that one captured graph serves every position.
@@ -24,7 +23,7 @@ enum Epi : int {
 };
 
 struct ProjArgs {
-    const uint32_t *w;   // pair-interleaved, byte-split weights (see layout.cu)
+    const uint32_t *w;   // unit-ordered, byte-split weights (see launch_pack_pairs)
     int K;               // input features
     int npairs;          // output row pairs
     const int16_t *x;    // input rows [kMaxRows][K]
@@ -45,6 +44,8 @@ struct ProjArgs {
     int q_pairs;         // pairs belonging to Q (local heads * hd/2)
     int kv_pairs;        // pairs of K (= of V) (kv_heads * hd/2)
     int max_seq;
+    int stages;          // shared-memory ring stages (gemv_stages)
+    int *error;          // device word: nonzero after a bounded wait expired
 };
 
 constexpr int kCluster = 8;         // CTAs per (row, query head) attention cluster
@@ -91,9 +92,9 @@ cudaError_t attn_configure(int max_smem_bytes);
 size_t attn_smem_bytes(int tpc, int hd);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
-size_t proj_smem_bytes(int rows_tmpl, int K);
 cudaError_t proj_configure(int max_smem_bytes);
-int proj_max_ctas_per_sm(int epi, int rows_tmpl, int K);
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages);
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem);
 
 // Weight layout kernel (model upload): slot s of the destination receives
 // dense row row_of_slot[s], columns [col0, col0+K), as K/2 32-bit words; word j

@@ -72,6 +72,7 @@ struct llmx_ctx {
     int16_t *q = nullptr, *att = nullptr, *act = nullptr;
     int64_t *partial = nullptr;
     Step *step = nullptr;
+    int *err = nullptr;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -107,11 +108,19 @@ int16_t *vc_layer(const llmx_ctx *c, uint32_t layer) {
 }
 const uint32_t *wl(const llmx_ctx *c, uint32_t layer) { return c->wbuf + (size_t)layer * c->layer_words; }
 
+constexpr int kProjSmem = 227 * 1024;
+
+// One persistent CTA per SM; the ring depth fills the shared memory left after
+// the activation rows (bounded so that the next kernel's CTA can co-reside).
 int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
-    const int want = (npairs + kWarps - 1) / kWarps;
-    int occ = proj_max_ctas_per_sm(0, rt, K);
-    if (occ < 1) occ = 1;
-    return std::max(1, std::min(want, c->nsm * occ));
+    (void)rt;
+    (void)K;
+    return std::max(1, std::min(c->nsm, npairs));
+}
+
+void set_stages(ProjArgs &a, int epi, int rt, int *err) {
+    a.stages = gemv_stages(rt, epi, a.K, kProjSmem);
+    a.error = err;
 }
 
 int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
@@ -219,19 +228,23 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     int16_t *out = c->hid[out_pair];
     const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
-        const ProjArgs a = qkv_args(c, layer, in);
+        ProjArgs a = qkv_args(c, layer, in);
+        set_stages(a, EPI_QKV, rt, c->err);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         CK(launch_attn(attn_args(c, layer), (int)rows, c->stream));
-        const ProjArgs o = o_args(c, layer, out, in);
+        ProjArgs o = o_args(c, layer, out, in);
+        set_stages(o, ge, rt, c->err);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
         c->launches += 3;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
         return LLMX_OK;
     }
     if (op == LLMX_OP_FFN_SUBLAYER) {
-        const ProjArgs g = gu_args(c, layer, in);
+        ProjArgs g = gu_args(c, layer, in);
+        set_stages(g, EPI_SILU, rt, c->err);
         CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
-        const ProjArgs d = down_args(c, layer, out, in);
+        ProjArgs d = down_args(c, layer, out, in);
+        set_stages(d, ge, rt, c->err);
         CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
         c->launches += 2;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
@@ -251,6 +264,18 @@ int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
     k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows);
     CK(cudaGetLastError());
     c->launches += 1;
+    return LLMX_OK;
+}
+
+// Kernels record an expired bounded wait in c->err; report and clear it.
+int check_device_error(llmx_ctx *c) {
+    int v = 0;
+    CK(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+        CK(cudaMemset(c->err, 0, sizeof(int)));
+        g_last_error = "a kernel's bounded wait expired (code " + std::to_string(v) + ")";
+        return LLMX_ERR_TIMEOUT;
+    }
     return LLMX_OK;
 }
 
@@ -364,7 +389,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->nsm = prop.multiProcessorCount;
     e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
-    e = proj_configure(200 * 1024);
+    e = proj_configure(kProjSmem);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
     e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd));
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
@@ -387,7 +412,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->att, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->act, kMaxRows * (size_t)c->Il)) || (rc = dalloc(c, &c->partial, kMaxRows * H)) ||
-        (rc = dalloc(c, &c->step, 1)))
+        (rc = dalloc(c, &c->step, 1)) || (rc = dalloc(c, &c->err, 1)))
         return bail(rc);
 
     // slot -> dense row tables of the pair-interleaved layout
@@ -573,7 +598,7 @@ int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint3
     if (rc) return rc;
     CK(cudaStreamSynchronize(c->stream));
     c->last_launches = c->launches - before;
-    return LLMX_OK;
+    return check_device_error(c);
 }
 
 int llmx_stack_async(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, uint32_t position,
@@ -606,6 +631,7 @@ int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t la
         CK(cudaMemcpyAsync(hidden_out, c->hid[include_final_norm ? 0 : 1], (size_t)rows * c->s.hidden * 2,
                            cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    if ((rc = check_device_error(c))) return rc;
     if (last) {
         const uint32_t op = include_final_norm ? LLMX_OP_FINAL_NORM : LLMX_OP_FFN_SUBLAYER;
         llmx_validate_task(&c->s, op, include_final_norm ? 0 : layer_begin + layer_count - 1, position, rows,
@@ -618,7 +644,7 @@ int llmx_synchronize(llmx_ctx *c) {
     if (!c) return LLMX_ERR_ARG;
     CK(cudaSetDevice(c->dev));
     CK(cudaStreamSynchronize(c->stream));
-    return LLMX_OK;
+    return check_device_error(c);
 }
 
 int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position, uint32_t rows, int iters,
@@ -643,20 +669,24 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         cur = (cur + 1) % (uint32_t)c->s.layers;
         switch (kernel) {
         case LLMX_KERNEL_QKV: {
-            const ProjArgs a = qkv_args(c, layer, in);
+            ProjArgs a = qkv_args(c, layer, in);
+            set_stages(a, EPI_QKV, rt, c->err);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
         case LLMX_KERNEL_ATTN: return launch_attn(attn_args(c, layer), (int)rows, c->stream);
         case LLMX_KERNEL_O: {
-            const ProjArgs o = o_args(c, layer, out, in);
+            ProjArgs o = o_args(c, layer, out, in);
+            set_stages(o, ge, rt, c->err);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
         }
         case LLMX_KERNEL_GATE_UP: {
-            const ProjArgs g = gu_args(c, layer, in);
+            ProjArgs g = gu_args(c, layer, in);
+            set_stages(g, EPI_SILU, rt, c->err);
             return launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream);
         }
         case LLMX_KERNEL_DOWN: {
-            const ProjArgs d = down_args(c, layer, out, in);
+            ProjArgs d = down_args(c, layer, out, in);
+            set_stages(d, ge, rt, c->err);
             return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
         }
         case LLMX_KERNEL_FINAL_NORM: {

@@ -155,6 +155,7 @@ const char *llmx_strerror(int code) {
     case LLMX_ERR_NOMEM: return "out of memory";
     case LLMX_ERR_IO: return "checkpoint file missing or wrong size";
     case LLMX_ERR_UNSUPPORTED: return "unsupported shape";
+    case LLMX_ERR_TIMEOUT: return "device wait timed out";
     default: return "unknown error";
     }
 }

@@ -23,7 +23,7 @@ LIB_PATH = os.path.join(HERE, "libllmx.so")
 
 OK = 0
 BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 3, 4, 5
-ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED = range(100, 108)
+ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED, ERR_TIMEOUT = range(100, 109)
 OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
 MAX_ROWS = 8
 KERNEL_QKV, KERNEL_ATTN, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(6)
