@@ -108,7 +108,7 @@ int16_t *vc_layer(const llmx_ctx *c, uint32_t layer) {
 }
 const uint32_t *wl(const llmx_ctx *c, uint32_t layer) { return c->wbuf + (size_t)layer * c->layer_words; }
 
-constexpr int kProjSmem = 227 * 1024;
+constexpr int kProjSmem = 226 * 1024;  // 227 KiB per CTA minus the kernels' static shared memory
 
 // One persistent CTA per SM; the ring depth fills the shared memory left after
 // the activation rows (bounded so that the next kernel's CTA can co-reside).
