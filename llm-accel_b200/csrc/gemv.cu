@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
     const int K = a.K, KV8 = K >> 3;
     const int unit_words = U * (K >> 1);
     const uint32_t unit_bytes = (uint32_t)unit_words * 4;
-    const int S = a.stages;
+    const int S = a.stages, C = a.consumers;  // C divides S: stage s is consumed only by warp s % C
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     char *ring = smem + 2 * kMaxStages * sizeof(uint64_t);
@@ -253,7 +253,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
     stage_rows<R>(a, xs, rows, tid);
     const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
 
-    for (int j = warp; j < nloc; j += kConsumers) {
+    // Unit j lives in stage j % S and is consumed by warp j % C.  Since C
+    // divides S, every stage has exactly one consumer warp, which waits on the
+    // stage's fills in order -- a parity wait is only unambiguous for the
+    // phase right after the one the waiter consumed last.
+    for (int j = warp; warp < C && j < nloc; j += C) {
         const int s = j % S;
         if (!__all_sync(0xffffffffu, mbar_wait(full + s, (j / S) & 1))) {  // warp-uniform decision
             if (lane == 0) atomicExch(a.error, 2);
@@ -353,14 +357,29 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages) {
     return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * U * K * 2 + (size_t)rows_tmpl * K * 2;
 }
 
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem) {
+// Ring depth S and consumer warps C (C in {8,4,2,1}, C divides S).  Decode
+// (few rows) prefers the deepest ring; blocks of >= 4 rows are compute-heavy
+// and prefer all eight consumer warps.
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int *consumers) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const size_t unit = (size_t)U * K * 2;
     int s = (int)(kRingBytes / unit);
     if (s > kMaxStages) s = kMaxStages;
-    if (s < 2) s = 2;
-    while (s > 2 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;
-    return s;
+    if (s < 1) s = 1;
+    while (s > 1 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;
+    int best_s = 1, best_c = 1;
+    for (int c = 1; c <= kConsumers; c *= 2) {
+        const int sc = s - s % c;
+        if (sc < c) continue;
+        const bool better = rows_tmpl >= 4 ? (c > best_c || (c == best_c && sc > best_s))
+                                           : (sc > best_s || (sc == best_s && c > best_c));
+        if (better) {
+            best_s = sc;
+            best_c = c;
+        }
+    }
+    *consumers = best_c;
+    return best_s;
 }
 
 template <int R, int EPI>

@@ -119,7 +119,7 @@ int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
 }
 
 void set_stages(ProjArgs &a, int epi, int rt, int *err) {
-    a.stages = gemv_stages(rt, epi, a.K, kProjSmem);
+    a.stages = gemv_stages(rt, epi, a.K, kProjSmem, &a.consumers);
     a.error = err;
 }
 
