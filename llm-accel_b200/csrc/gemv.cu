@@ -31,7 +31,6 @@ namespace llmx {
 
 constexpr int kConsumers = 8;                       // consumer warps
 constexpr int kGemvThreads = (kConsumers + 1) * 32; // + one producer warp
-constexpr int kRingBytes = 96 * 1024;               // target weight bytes in flight per SM
 constexpr int kMaxStages = 32;
 constexpr uint32_t kSpinLimit = 1u << 26;           // bounded mbarrier waits (seconds of polling)
 
@@ -360,10 +359,10 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages) {
 // Ring depth S and consumer warps C (C in {8,4,2,1}, C divides S).  Decode
 // (few rows) prefers the deepest ring; blocks of >= 4 rows are compute-heavy
 // and prefer all eight consumer warps.
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int *consumers) {
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *consumers) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const size_t unit = (size_t)U * K * 2;
-    int s = (int)(kRingBytes / unit);
+    int s = (int)(ring_bytes / unit);
     if (s > kMaxStages) s = kMaxStages;
     if (s < 1) s = 1;
     while (s > 1 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -73,6 +74,7 @@ struct llmx_ctx {
     int64_t *partial = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
+    int ring_kb = 96, gemv_ctas_per_sm = 1;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -110,17 +112,25 @@ const uint32_t *wl(const llmx_ctx *c, uint32_t layer) { return c->wbuf + (size_t
 
 constexpr int kProjSmem = 226 * 1024;  // 227 KiB per CTA minus the kernels' static shared memory
 
-// One persistent CTA per SM; the ring depth fills the shared memory left after
-// the activation rows (bounded so that the next kernel's CTA can co-reside).
+// Persistent projection CTAs: gemv_ctas_per_sm per SM (LLMX_GEMV_CTAS_PER_SM),
+// each streaming through a ring of about ring_kb KiB (LLMX_RING_KB).
 int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
     (void)rt;
     (void)K;
-    return std::max(1, std::min(c->nsm, npairs));
+    return std::max(1, std::min(c->nsm * c->gemv_ctas_per_sm, npairs));
 }
 
-void set_stages(ProjArgs &a, int epi, int rt, int *err) {
-    a.stages = gemv_stages(rt, epi, a.K, kProjSmem, &a.consumers);
-    a.error = err;
+void set_stages(llmx_ctx *c, ProjArgs &a, int epi, int rt) {
+    const int smem = kProjSmem / c->gemv_ctas_per_sm - 1024;
+    a.stages = gemv_stages(rt, epi, a.K, smem, c->ring_kb * 1024, &a.consumers);
+    a.error = c->err;
+}
+
+int env_int(const char *name, int def, int lo, int hi) {
+    const char *v = std::getenv(name);
+    if (!v || !*v) return def;
+    const int x = std::atoi(v);
+    return x < lo ? lo : (x > hi ? hi : x);
 }
 
 int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
@@ -229,11 +239,11 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         ProjArgs a = qkv_args(c, layer, in);
-        set_stages(a, EPI_QKV, rt, c->err);
+        set_stages(c, a, EPI_QKV, rt);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         CK(launch_attn(attn_args(c, layer), (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
-        set_stages(o, ge, rt, c->err);
+        set_stages(c, o, ge, rt);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
         c->launches += 3;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
@@ -241,10 +251,10 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     }
     if (op == LLMX_OP_FFN_SUBLAYER) {
         ProjArgs g = gu_args(c, layer, in);
-        set_stages(g, EPI_SILU, rt, c->err);
+        set_stages(c, g, EPI_SILU, rt);
         CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
         ProjArgs d = down_args(c, layer, out, in);
-        set_stages(d, ge, rt, c->err);
+        set_stages(c, d, ge, rt);
         CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
         c->launches += 2;
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
@@ -377,6 +387,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->c0 = tp_rank * c->Il;
     c->tpc_max = ((s.max_seq + kTile - 1) / kTile + kCluster - 1) / kCluster;
     c->layer_loaded.assign(s.layers, false);
+    c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
+    c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     auto bail = [&](int code) {
         release(c);
         return code;
@@ -670,23 +682,23 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         switch (kernel) {
         case LLMX_KERNEL_QKV: {
             ProjArgs a = qkv_args(c, layer, in);
-            set_stages(a, EPI_QKV, rt, c->err);
+            set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
         case LLMX_KERNEL_ATTN: return launch_attn(attn_args(c, layer), (int)rows, c->stream);
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
-            set_stages(o, ge, rt, c->err);
+            set_stages(c, o, ge, rt);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
         }
         case LLMX_KERNEL_GATE_UP: {
             ProjArgs g = gu_args(c, layer, in);
-            set_stages(g, EPI_SILU, rt, c->err);
+            set_stages(c, g, EPI_SILU, rt);
             return launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream);
         }
         case LLMX_KERNEL_DOWN: {
             ProjArgs d = down_args(c, layer, out, in);
-            set_stages(d, ge, rt, c->err);
+            set_stages(c, d, ge, rt);
             return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
         }
         case LLMX_KERNEL_FINAL_NORM: {
