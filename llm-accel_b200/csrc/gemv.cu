@@ -29,8 +29,13 @@
 
 namespace llmx {
 
-constexpr int kConsumers = 8;                       // consumer warps
-constexpr int kGemvThreads = (kConsumers + 1) * 32; // + one producer warp
+// Consumer warps per CTA: 16 for decode-sized row counts (latency hiding),
+// 8 for blocks of >= 4 rows (register budget of the 8-row accumulators).
+template <int R>
+struct Warps {
+    static constexpr int kConsumers = R <= 2 ? 16 : 8;
+    static constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
+};
 constexpr int kMaxStages = 32;
 constexpr uint32_t kSpinLimit = 1u << 26;           // bounded mbarrier waits (seconds of polling)
 
@@ -69,8 +74,9 @@ static __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+template <int CW>
 static __device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 }
 
 // golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
@@ -116,7 +122,8 @@ static __device__ __forceinline__ int64_t warp_reduce_n(int64_t (&v)[N], int lan
 // when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
 template <int R>
 static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int tid) {
-    constexpr int T = kConsumers * 32;
+    constexpr int CW = Warps<R>::kConsumers;
+    constexpr int T = CW * 32;
     const int K = a.K, KV8 = K >> 3;
     __shared__ int32_t inv_rms_s[kMaxRows];
     if (a.norm != nullptr) {
@@ -124,7 +131,7 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
             // recip(fm(K)) == 0: mean == 0 for every input, inv_rms is a constant
             if (tid < R) inv_rms_s[tid] = a.inv_rms_const;
         } else {
-            __shared__ int64_t red[kConsumers][kMaxRows];
+            __shared__ int64_t red[CW][kMaxRows];
             int64_t part[R];
 #pragma unroll
             for (int r = 0; r < R; r++) part[r] = 0;
@@ -143,15 +150,15 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
             if ((tid & 31) == 0)
 #pragma unroll
                 for (int r = 0; r < R; r++) red[tid >> 5][r] = part[r];
-            consumer_sync();
+            consumer_sync<CW>();
             if (tid < R) {
                 int64_t sum = 0;
-                for (int w = 0; w < kConsumers; w++) sum += red[w][tid];
+                for (int w = 0; w < CW; w++) sum += red[w][tid];
                 // saturating running sum == min(total, INT32_MAX): every term is >= 0
                 inv_rms_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
             }
         }
-        consumer_sync();
+        consumer_sync<CW>();
         const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
         const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm);
         for (int i = tid; i < R * KV8; i += T) {
@@ -177,7 +184,7 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
         for (int i = tid; i < R * KV8; i += T)
             reinterpret_cast<uint4 *>(xs)[i] = (i / KV8) < rows ? x4[i] : make_uint4(0, 0, 0, 0);
     }
-    consumer_sync();
+    consumer_sync<CW>();
 }
 
 template <int R, int EPI>
@@ -191,10 +198,88 @@ static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) 
     u1 = (int)((int64_t)nunits * (blockIdx.x + 1) / gridDim.x);
 }
 
-template <int R, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
+// One unit's dot products against R activation rows, accumulated exactly.
+// VPL > 0: K == 256 * VPL, every lane takes VPL 16-byte vectors per row (fully
+// unrolled, no predicates); VPL == 0: any K, 16-vector chunks with int32
+// partials flushed to int64 after each chunk.
+//   |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29 per chunk.
+template <int R, int U, int VPL>
+static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, const uint4 *__restrict__ xs4,
+                                                 const uint4 (&xr)[VPL > 0 ? VPL : 1], int KV8, int lane,
+                                                 int64_t (&acc)[U * R]) {
+    constexpr int N = U * R;
+#pragma unroll
+    for (int i = 0; i < N; i++) acc[i] = 0;
+    if constexpr (VPL > 0) {
+        int lo[N], hi[N];
+#pragma unroll
+        for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
+#pragma unroll
+        for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) {
+            const int v = k * 32 + lane;
+            uint4 w[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const uint4 x = R == 1 ? xr[k] : xs4[r * KV8 + v];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int i = r * U + u;
+                    lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
+                    hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
+                    lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
+                    hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
+                    lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
+                    hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
+                    lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
+                    hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < N; i++) acc[i] = (int64_t)hi[i] * 256 + lo[i];
+    } else {
+    for (int v0 = 0; v0 < KV8; v0 += 16 * 32) {
+        int lo[N], hi[N];
+#pragma unroll
+        for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
+#pragma unroll 4
+        for (int k = 0; k < 16; k++) {
+            const int v = v0 + k * 32 + lane;
+            if (v < KV8) {
+                uint4 w[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const uint4 x = xs4[r * KV8 + v];
+#pragma unroll
+                    for (int u = 0; u < U; u++) {
+                        const int i = r * U + u;
+                        lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
+                        hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
+                        lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
+                        hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
+                        lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
+                        hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
+                        lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
+                        hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
+    }
+    }
+}
+
+template <int R, int EPI, int VPL>
+__global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a) {
     constexpr int U = GemvTraits<R, EPI>::U;
     constexpr int N = U * R;  // int64 sums per unit
+    constexpr int CW = Warps<R>::kConsumers;
     extern __shared__ __align__(128) char smem[];
     const int K = a.K, KV8 = K >> 3;
     const int unit_words = U * (K >> 1);
@@ -219,7 +304,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
     }
     __syncthreads();
 
-    if (warp == kConsumers) {  // ---------------- producer warp -------------
+    if (warp == CW) {  // ---------------- producer warp -------------
         if (lane == 0) {
             const char *src = reinterpret_cast<const char *>(a.w) + (size_t)u0 * unit_bytes;
             bool ok = true;
@@ -244,13 +329,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
     }
 
     // ---------------- consumer warps ----------------------------------------
-    const int tid = threadIdx.x;  // 0 .. 255
+    const int tid = threadIdx.x;
     pdl_wait();
     pdl_trigger();
     const Step st = *a.step;
     const int rows = st.rows;
     stage_rows<R>(a, xs, rows, tid);
     const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
+    uint4 xr[VPL > 0 ? VPL : 1];  // 1-row decode: this lane's activation vectors stay in registers
+    if (R == 1 && VPL > 0) {
+#pragma unroll
+        for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) xr[k] = xs4[k * 32 + lane];
+    }
 
     // Unit j lives in stage j % S and is consumed by warp j % C.  Since C
     // divides S, every stage has exactly one consumer warp, which waits on the
@@ -262,43 +352,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const ProjArgs a) {
             if (lane == 0) atomicExch(a.error, 2);
             break;
         }
-        const uint4 *wv = reinterpret_cast<const uint4 *>(ring + (size_t)s * unit_bytes);
         int64_t acc[N];
-#pragma unroll
-        for (int i = 0; i < N; i++) acc[i] = 0;
-        for (int v0 = 0; v0 < KV8; v0 += 16 * 32) {  // int32 partials flushed every 16 vectors per lane
-            int lo[N], hi[N];
-#pragma unroll
-            for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
-#pragma unroll 4
-            for (int k = 0; k < 16; k++) {
-                const int v = v0 + k * 32 + lane;
-                if (v < KV8) {
-                    uint4 w[U];
-#pragma unroll
-                    for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
-#pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        const uint4 x = xs4[r * KV8 + v];
-#pragma unroll
-                        for (int u = 0; u < U; u++) {
-                            const int i = r * U + u;
-                            lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
-                            hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
-                            lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
-                            hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
-                            lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
-                            hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
-                            lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
-                            hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
-                        }
-                    }
-                }
-            }
-            // |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29
-#pragma unroll
-            for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
-        }
+        unit_dots<R, U, VPL>(reinterpret_cast<const uint4 *>(ring + (size_t)s * unit_bytes), xs4, xr, KV8, lane,
+                             acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + s);  // stage free for the producer
 
@@ -356,9 +412,8 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages) {
     return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * U * K * 2 + (size_t)rows_tmpl * K * 2;
 }
 
-// Ring depth S and consumer warps C (C in {8,4,2,1}, C divides S).  Decode
-// (few rows) prefers the deepest ring; blocks of >= 4 rows are compute-heavy
-// and prefer all eight consumer warps.
+// Ring depth S and consumer warps C (a power of two up to the kernel's consumer
+// warps, dividing S): the most consumers, then the deepest ring.
 int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *consumers) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const size_t unit = (size_t)U * K * 2;
@@ -366,13 +421,12 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
     if (s > kMaxStages) s = kMaxStages;
     if (s < 1) s = 1;
     while (s > 1 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;
+    const int cmax = rows_tmpl <= 2 ? 16 : 8;
     int best_s = 1, best_c = 1;
-    for (int c = 1; c <= kConsumers; c *= 2) {
+    for (int c = 1; c <= cmax; c *= 2) {
         const int sc = s - s % c;
         if (sc < c) continue;
-        const bool better = rows_tmpl >= 4 ? (c > best_c || (c == best_c && sc > best_s))
-                                           : (sc > best_s || (sc == best_s && c > best_c));
-        if (better) {
+        if (c > best_c || (c == best_c && sc > best_s)) {
             best_s = sc;
             best_c = c;
         }
@@ -381,13 +435,13 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
     return best_s;
 }
 
-template <int R, int EPI>
-static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
+template <int R, int EPI, int VPL>
+static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     ProjArgs c = a;
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kGemvThreads);
+    cfg.blockDim = dim3(Warps<R>::kThreads);
     cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -395,7 +449,14 @@ static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI>, args);
+    return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI, VPL>, args);
+}
+
+// K = 2048 (any projection with hidden inputs): fully unrolled path.
+template <int R, int EPI>
+static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
+    if (a.K == 2048) return launch_gemv_v<R, EPI, 8>(a, grid, st);
+    return launch_gemv_v<R, EPI, 0>(a, grid, st);
 }
 
 template <int EPI>
@@ -417,13 +478,20 @@ cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cud
     }
 }
 
+template <int R, int EPI>
+static cudaError_t configure_r(int bytes) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e) return e;
+    return cudaFuncSetAttribute(k_gemv<R, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 template <int EPI>
 static cudaError_t configure_epi(int bytes) {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(k_gemv<1, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
-    if ((e = cudaFuncSetAttribute(k_gemv<2, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
-    if ((e = cudaFuncSetAttribute(k_gemv<4, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
-    return cudaFuncSetAttribute(k_gemv<8, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if ((e = configure_r<1, EPI>(bytes))) return e;
+    if ((e = configure_r<2, EPI>(bytes))) return e;
+    if ((e = configure_r<4, EPI>(bytes))) return e;
+    return configure_r<8, EPI>(bytes);
 }
 
 cudaError_t proj_configure(int max_smem_bytes) {

@@ -110,7 +110,7 @@ int16_t *vc_layer(const llmx_ctx *c, uint32_t layer) {
 }
 const uint32_t *wl(const llmx_ctx *c, uint32_t layer) { return c->wbuf + (size_t)layer * c->layer_words; }
 
-constexpr int kProjSmem = 226 * 1024;  // 227 KiB per CTA minus the kernels' static shared memory
+constexpr int kProjSmem = 225 * 1024;  // 227 KiB per CTA minus the kernels' static shared memory
 
 // Persistent projection CTAs: gemv_ctas_per_sm per SM (LLMX_GEMV_CTAS_PER_SM),
 // each streaming through a ring of about ring_kb KiB (LLMX_RING_KB).
