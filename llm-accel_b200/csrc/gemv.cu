@@ -284,21 +284,28 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     const int K = a.K, KV8 = K >> 3;
     const int unit_words = U * (K >> 1);
     const uint32_t unit_bytes = (uint32_t)unit_words * 4;
-    const int S = a.stages, C = a.consumers;  // C divides S: stage s is consumed only by warp s % C
+    // G stages, each holding one chunk of B consecutive units (one bulk copy);
+    // consumer warp w = g*B + b belongs to group g, which owns stage g and takes
+    // unit b of every chunk j = g, g+G, g+2G, ...  Every stage is thus waited on
+    // by the same warps, in phase order.
+    const int G = a.stages, B = a.units_per_chunk, C = G * B;
+    const int S = G;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     char *ring = smem + 2 * kMaxStages * sizeof(uint64_t);
-    int16_t *xs = reinterpret_cast<int16_t *>(ring + (size_t)S * unit_bytes);
+    const uint32_t chunk_bytes = unit_bytes * (uint32_t)B;
+    int16_t *xs = reinterpret_cast<int16_t *>(ring + (size_t)S * chunk_bytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = a.npairs * 2 / U;
     int u0, u1;
     unit_range(nunits, u0, u1);
     const int nloc = u1 - u0;
+    const int nchunks = (nloc + B - 1) / B;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1);
+            mbar_init(empty + s, (uint32_t)B);  // every warp of the owning group arrives
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -308,21 +315,27 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
         if (lane == 0) {
             const char *src = reinterpret_cast<const char *>(a.w) + (size_t)u0 * unit_bytes;
             bool ok = true;
-            for (int j = 0; j < nloc; j++) {
+            int issued = 0;
+            for (int j = 0; j < nchunks; j++) {
                 const int s = j % S;
                 if (j >= S && !mbar_wait(empty + s, ((j / S) - 1) & 1)) {
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(full + s, unit_bytes);
-                bulk_g2s(ring + (size_t)s * unit_bytes, src + (size_t)j * unit_bytes, unit_bytes, full + s);
+                const uint32_t bytes = (uint32_t)min(B, nloc - j * B) * unit_bytes;
+                mbar_expect_tx(full + s, bytes);
+                bulk_g2s(ring + (size_t)s * chunk_bytes, src + (size_t)j * chunk_bytes, bytes, full + s);
+                issued = j + 1;
                 if (j == S - 1) pdl_wait();  // ring primed before waiting on the producer kernel
             }
-            if (nloc < S) pdl_wait();
+            if (nchunks < S) pdl_wait();
             if (!ok) {
                 atomicExch(a.error, 1);
-                // drain: wait (bounded) for every copy this thread issued to land
-                for (int s = 0; s < S && s < nloc; s++) (void)mbar_wait(full + s, ((nloc - 1 - s) / S) & 1);
+                // drain: wait (bounded) for the last fill of every stage this thread issued
+                for (int s = 0; s < S && s < issued; s++) {
+                    const int last = s + ((issued - 1 - s) / S) * S;
+                    (void)mbar_wait(full + s, (last / S) & 1);
+                }
             }
         }
         return;
@@ -342,25 +355,27 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
         for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) xr[k] = xs4[k * 32 + lane];
     }
 
-    // Unit j lives in stage j % S and is consumed by warp j % C.  Since C
-    // divides S, every stage has exactly one consumer warp, which waits on the
-    // stage's fills in order -- a parity wait is only unambiguous for the
-    // phase right after the one the waiter consumed last.
-    for (int j = warp; warp < C && j < nloc; j += C) {
+    // A parity wait is only unambiguous for the phase right after the one the
+    // waiter consumed last, so each group waits on its own stage chunk by chunk.
+    const int grp = warp / B, slot = warp - grp * B;
+    for (int j = grp; warp < C && j < nchunks; j += G) {
         const int s = j % S;
         if (!__all_sync(0xffffffffu, mbar_wait(full + s, (j / S) & 1))) {  // warp-uniform decision
             if (lane == 0) atomicExch(a.error, 2);
             break;
         }
+        const int jl = j * B + slot;  // local unit index
         int64_t acc[N];
-        unit_dots<R, U, VPL>(reinterpret_cast<const uint4 *>(ring + (size_t)s * unit_bytes), xs4, xr, KV8, lane,
-                             acc);
+        if (jl < nloc)
+            unit_dots<R, U, VPL>(reinterpret_cast<const uint4 *>(ring + (size_t)s * chunk_bytes + (size_t)slot * unit_bytes),
+                                 xs4, xr, KV8, lane, acc);
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + s);  // stage free for the producer
+        if (lane == 0) mbar_arrive(empty + s);  // this warp's part of the stage is free
+        if (jl >= nloc) continue;
 
         int idx;
         const int64_t tot = warp_reduce_n<N>(acc, lane, idx);
-        const int unit = u0 + j;
+        const int unit = u0 + jl;
         if (U == 2) {
             constexpr int kPartnerBit = 32 / N;
             const int64_t other = __shfl_sync(0xffffffffu, tot, lane | kPartnerBit);
@@ -407,32 +422,31 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     }
 }
 
-size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages) {
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
-    return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * U * K * 2 + (size_t)rows_tmpl * K * 2;
+    return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * units_per_chunk * U * K * 2 +
+           (size_t)rows_tmpl * K * 2;
 }
 
-// Ring depth S and consumer warps C (a power of two up to the kernel's consumer
-// warps, dividing S): the most consumers, then the deepest ring.
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *consumers) {
+// Ring plan.  1-D bulk copies only stream at full HBM rate when each copy is
+// large (>= 16 KiB on B200: 8 KiB copies cap near 4 TB/s), so a stage holds B
+// consecutive units making a ~32 KiB chunk, and G stages form the ring; the
+// consumer warps are G groups of B.  Limits: G*B <= consumer warps of the
+// kernel, G >= 2 (double buffering), shared memory within max_smem.
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
-    const size_t unit = (size_t)U * K * 2;
-    int s = (int)(ring_bytes / unit);
-    if (s > kMaxStages) s = kMaxStages;
-    if (s < 1) s = 1;
-    while (s > 1 && gemv_smem_bytes(rows_tmpl, epi, K, s) > (size_t)max_smem) s--;
+    const int unit = U * K * 2;
     const int cmax = rows_tmpl <= 2 ? 16 : 8;
-    int best_s = 1, best_c = 1;
-    for (int c = 1; c <= cmax; c *= 2) {
-        const int sc = s - s % c;
-        if (sc < c) continue;
-        if (c > best_c || (c == best_c && sc > best_s)) {
-            best_s = sc;
-            best_c = c;
-        }
-    }
-    *consumers = best_c;
-    return best_s;
+    int B = (32 * 1024) / unit;
+    if (B < 1) B = 1;
+    if (B > cmax / 2) B = cmax / 2;
+    int G = ring_bytes / (B * unit);
+    if (G > cmax / B) G = cmax / B;
+    if (G < 2) G = 2;
+    while (G > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B) > (size_t)max_smem) G--;
+    while (B > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B) > (size_t)max_smem) B--;
+    *units_per_chunk = B;
+    return G;
 }
 
 template <int R, int EPI, int VPL>
@@ -442,7 +456,7 @@ static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(Warps<R>::kThreads);
-    cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages);
+    cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages, a.units_per_chunk);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

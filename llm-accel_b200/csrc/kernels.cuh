@@ -44,8 +44,8 @@ struct ProjArgs {
     int q_pairs;         // pairs belonging to Q (local heads * hd/2)
     int kv_pairs;        // pairs of K (= of V) (kv_heads * hd/2)
     int max_seq;
-    int stages;          // shared-memory ring stages S (gemv_stages)
-    int consumers;       // consumer warps C (divides S)
+    int stages;          // shared-memory ring stages G (gemv_stages)
+    int units_per_chunk; // units B per stage / bulk copy; G*B consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
 };
 
@@ -94,8 +94,8 @@ size_t attn_smem_bytes(int tpc, int hd);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 cudaError_t proj_configure(int max_smem_bytes);
-size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages);
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *consumers);
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk);
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk);
 
 // Weight layout kernel (model upload): slot s of the destination receives
 // dense row row_of_slot[s], columns [col0, col0+K), as K/2 32-bit words; word j
