@@ -74,9 +74,9 @@ static __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-template <int CW>
+// Named barrier over the consumer warps (the producer warp is the last warp).
 static __device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 32) : "memory");
 }
 
 // golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
@@ -122,8 +122,8 @@ static __device__ __forceinline__ int64_t warp_reduce_n(int64_t (&v)[N], int lan
 // when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
 template <int R>
 static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int tid) {
-    constexpr int CW = Warps<R>::kConsumers;
-    constexpr int T = CW * 32;
+    constexpr int CW = Warps<R>::kConsumers;  // upper bound of the consumer warps
+    const int T = blockDim.x - 32, cw = T / 32;
     const int K = a.K, KV8 = K >> 3;
     __shared__ int32_t inv_rms_s[kMaxRows];
     if (a.norm != nullptr) {
@@ -150,15 +150,15 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
             if ((tid & 31) == 0)
 #pragma unroll
                 for (int r = 0; r < R; r++) red[tid >> 5][r] = part[r];
-            consumer_sync<CW>();
+            consumer_sync();
             if (tid < R) {
                 int64_t sum = 0;
-                for (int w = 0; w < CW; w++) sum += red[w][tid];
+                for (int w = 0; w < cw; w++) sum += red[w][tid];
                 // saturating running sum == min(total, INT32_MAX): every term is >= 0
                 inv_rms_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
             }
         }
-        consumer_sync<CW>();
+        consumer_sync();
         const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
         const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm);
         for (int i = tid; i < R * KV8; i += T) {
@@ -184,7 +184,7 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
         for (int i = tid; i < R * KV8; i += T)
             reinterpret_cast<uint4 *>(xs)[i] = (i / KV8) < rows ? x4[i] : make_uint4(0, 0, 0, 0);
     }
-    consumer_sync<CW>();
+    consumer_sync();
 }
 
 template <int R, int EPI>
@@ -200,12 +200,12 @@ static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) 
 
 // One unit's dot products against R activation rows, accumulated exactly.
 // VPL > 0: K == 256 * VPL, every lane takes VPL 16-byte vectors per row (fully
-// unrolled, no predicates); VPL == 0: any K, 16-vector chunks with int32
-// partials flushed to int64 after each chunk.
-//   |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29 per chunk.
+// unrolled, no predicates; K = 2048 -> 8, K = 11008 -> 43); VPL == 0: any K,
+// 16-vector chunks.  The int32 partials are flushed to int64 every 16 vectors:
+//   |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29 per flush.
 template <int R, int U, int VPL>
 static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, const uint4 *__restrict__ xs4,
-                                                 const uint4 (&xr)[VPL > 0 ? VPL : 1], int KV8, int lane,
+                                                 const uint4 (&xr)[8], int KV8, int lane,
                                                  int64_t (&acc)[U * R]) {
     constexpr int N = U * R;
 #pragma unroll
@@ -216,13 +216,20 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
         for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
 #pragma unroll
         for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) {
+            if (k > 0 && k % 16 == 0) {  // flush the int32 partials every 16 vectors
+#pragma unroll
+                for (int i = 0; i < N; i++) {
+                    acc[i] += (int64_t)hi[i] * 256 + lo[i];
+                    lo[i] = hi[i] = 0;
+                }
+            }
             const int v = k * 32 + lane;
             uint4 w[U];
 #pragma unroll
             for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
 #pragma unroll
             for (int r = 0; r < R; r++) {
-                const uint4 x = R == 1 ? xr[k] : xs4[r * KV8 + v];
+                const uint4 x = (R == 1 && VPL <= 8) ? xr[k < 8 ? k : 0] : xs4[r * KV8 + v];
 #pragma unroll
                 for (int u = 0; u < U; u++) {
                     const int i = r * U + u;
@@ -238,7 +245,7 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
             }
         }
 #pragma unroll
-        for (int i = 0; i < N; i++) acc[i] = (int64_t)hi[i] * 256 + lo[i];
+        for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
     } else {
     for (int v0 = 0; v0 < KV8; v0 += 16 * 32) {
         int lo[N], hi[N];
@@ -279,7 +286,6 @@ template <int R, int EPI, int VPL>
 __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a) {
     constexpr int U = GemvTraits<R, EPI>::U;
     constexpr int N = U * R;  // int64 sums per unit
-    constexpr int CW = Warps<R>::kConsumers;
     extern __shared__ __align__(128) char smem[];
     const int K = a.K, KV8 = K >> 3;
     const int unit_words = U * (K >> 1);
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     }
     __syncthreads();
 
-    if (warp == CW) {  // ---------------- producer warp -------------
+    if (warp == (int)(blockDim.x >> 5) - 1) {  // ---------------- producer warp -------------
         if (lane == 0) {
             const char *src = reinterpret_cast<const char *>(a.w) + (size_t)u0 * unit_bytes;
             bool ok = true;
@@ -349,10 +355,11 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     const int rows = st.rows;
     stage_rows<R>(a, xs, rows, tid);
     const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
-    uint4 xr[VPL > 0 ? VPL : 1];  // 1-row decode: this lane's activation vectors stay in registers
-    if (R == 1 && VPL > 0) {
+    uint4 xr[8];  // 1-row decode with K <= 2048: this lane's activation vectors stay in registers
+    if (R == 1 && VPL > 0 && VPL <= 8) {
 #pragma unroll
-        for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) xr[k] = xs4[k * 32 + lane];
+        for (int k = 0; k < 8; k++)
+            if (k < VPL) xr[k] = xs4[k * 32 + lane];
     }
 
     // A parity wait is only unambiguous for the phase right after the one the
@@ -455,7 +462,7 @@ static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(Warps<R>::kThreads);
+    cfg.blockDim = dim3((a.stages * a.units_per_chunk + 1) * 32);  // consumer groups + producer
     cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages, a.units_per_chunk);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -466,10 +473,12 @@ static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI, VPL>, args);
 }
 
-// K = 2048 (any projection with hidden inputs): fully unrolled path.
+// Fully unrolled paths for the Qwen2.5-3B input widths: K = 2048 (hidden) and
+// K = 11008 (FFN, single GPU); everything else takes the generic loop.
 template <int R, int EPI>
 static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
     if (a.K == 2048) return launch_gemv_v<R, EPI, 8>(a, grid, st);
+    if ((EPI == EPI_RESID || EPI == EPI_PARTIAL) && a.K == 11008) return launch_gemv_v<R, EPI, 43>(a, grid, st);
     return launch_gemv_v<R, EPI, 0>(a, grid, st);
 }
 
@@ -496,6 +505,10 @@ template <int R, int EPI>
 static cudaError_t configure_r(int bytes) {
     cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e) return e;
+    if (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
+        e = cudaFuncSetAttribute(k_gemv<R, EPI, 43>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e) return e;
+    }
     return cudaFuncSetAttribute(k_gemv<R, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
