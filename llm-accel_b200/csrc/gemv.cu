@@ -478,7 +478,8 @@ static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
 template <int R, int EPI>
 static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
     if (a.K == 2048) return launch_gemv_v<R, EPI, 8>(a, grid, st);
-    if ((EPI == EPI_RESID || EPI == EPI_PARTIAL) && a.K == 11008) return launch_gemv_v<R, EPI, 43>(a, grid, st);
+    if (R <= 2 && (EPI == EPI_RESID || EPI == EPI_PARTIAL) && a.K == 11008)
+        return launch_gemv_v<R, EPI, 43>(a, grid, st);
     return launch_gemv_v<R, EPI, 0>(a, grid, st);
 }
 
@@ -505,7 +506,7 @@ template <int R, int EPI>
 static cudaError_t configure_r(int bytes) {
     cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e) return e;
-    if (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
+    if (R <= 2 && (EPI == EPI_RESID || EPI == EPI_PARTIAL)) {
         e = cudaFuncSetAttribute(k_gemv<R, EPI, 43>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
         if (e) return e;
     }
