@@ -8,8 +8,8 @@
 // B200 mapping.  One persistent CTA per SM owns a contiguous slice of the
 // weight matrix (whole "units": one output row, or a RoPE / gate-up pair of
 // rows).  A producer thread streams the slice through a shared-memory ring
-// with 1-D bulk copies (cp.async.bulk, completion on an mbarrier); eight
-// consumer warps take units round-robin, read weights and activations with
+// with 1-D bulk copies (cp.async.bulk, completion on an mbarrier); consumer
+// warps own fixed ring stages, read weights and activations with
 // 128-bit shared loads and form exact products with the dp2a pipe (weights
 // pre-split into unsigned low / signed high bytes, activations packed int16
 // pairs), so every MAC is exact and the reduction order is free.  The producer
@@ -203,9 +203,11 @@ static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) 
 // unrolled, no predicates; K = 2048 -> 8, K = 11008 -> 43); VPL == 0: any K,
 // 16-vector chunks.  The int32 partials are flushed to int64 every 16 vectors:
 //   |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29 per flush.
-template <int R, int U, int VPL>
+// P > 1: the unit is shared by P warps; warp `part` takes every P-th group of
+// 32 vectors, and the P partial sums are added afterwards (exact int64).
+template <int R, int U, int VPL, int P>
 static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, const uint4 *__restrict__ xs4,
-                                                 const uint4 (&xr)[8], int KV8, int lane,
+                                                 const uint4 (&xr)[8], int KV8, int lane, int part,
                                                  int64_t (&acc)[U * R]) {
     constexpr int N = U * R;
 #pragma unroll
@@ -214,9 +216,12 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
         int lo[N], hi[N];
 #pragma unroll
         for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
+        constexpr int KI = ((VPL > 0 ? VPL : 1) + P - 1) / P;  // vector groups of this warp
 #pragma unroll
-        for (int k = 0; k < (VPL > 0 ? VPL : 1); k++) {
-            if (k > 0 && k % 16 == 0) {  // flush the int32 partials every 16 vectors
+        for (int ki = 0; ki < KI; ki++) {
+            const int k = P == 1 ? ki : ki * P + part;
+            if (P > 1 && ki == KI - 1 && k >= VPL) break;
+            if (ki > 0 && ki % 16 == 0) {  // flush the int32 partials every 16 vectors
 #pragma unroll
                 for (int i = 0; i < N; i++) {
                     acc[i] += (int64_t)hi[i] * 256 + lo[i];
@@ -229,7 +234,7 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
             for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
 #pragma unroll
             for (int r = 0; r < R; r++) {
-                const uint4 x = (R == 1 && VPL <= 8) ? xr[k < 8 ? k : 0] : xs4[r * KV8 + v];
+                const uint4 x = (R == 1 && VPL <= 8 && P == 1) ? xr[k < 8 ? k : 0] : xs4[r * KV8 + v];
 #pragma unroll
                 for (int u = 0; u < U; u++) {
                     const int i = r * U + u;
@@ -247,13 +252,13 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
 #pragma unroll
         for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
     } else {
-    for (int v0 = 0; v0 < KV8; v0 += 16 * 32) {
+    for (int v0 = part * 32; v0 < KV8; v0 += 16 * 32 * P) {
         int lo[N], hi[N];
 #pragma unroll
         for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
 #pragma unroll 4
         for (int k = 0; k < 16; k++) {
-            const int v = v0 + k * 32 + lane;
+            const int v = v0 + k * 32 * P + lane;
             if (v < KV8) {
                 uint4 w[U];
 #pragma unroll
@@ -282,7 +287,7 @@ static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, c
     }
 }
 
-template <int R, int EPI, int VPL>
+template <int R, int EPI, int VPL, int P>
 __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a) {
     constexpr int U = GemvTraits<R, EPI>::U;
     constexpr int N = U * R;  // int64 sums per unit
@@ -291,16 +296,24 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     const int unit_words = U * (K >> 1);
     const uint32_t unit_bytes = (uint32_t)unit_words * 4;
     // G stages, each holding one chunk of B consecutive units (one bulk copy);
-    // consumer warp w = g*B + b belongs to group g, which owns stage g and takes
-    // unit b of every chunk j = g, g+G, g+2G, ...  Every stage is thus waited on
-    // by the same warps, in phase order.
-    const int G = a.stages, B = a.units_per_chunk, C = G * B;
+    // consumer warp w = (g*B + b)*P + p belongs to group g, which owns stage g,
+    // and takes part p of unit b of every chunk j = g, g+G, g+2G, ...  Every
+    // stage is thus waited on by the same warps, in phase order.
+    const int G = a.stages, B = a.units_per_chunk, C = G * B * P;
     const int S = G;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     char *ring = smem + 2 * kMaxStages * sizeof(uint64_t);
     const uint32_t chunk_bytes = unit_bytes * (uint32_t)B;
     int16_t *xs = reinterpret_cast<int16_t *>(ring + (size_t)S * chunk_bytes);
+    // P > 1: per (round parity, unit slot) int64 sums of the P parts and arrival
+    // counters; the last part to arrive runs the epilogue and clears the slot.
+    int64_t *cacc = reinterpret_cast<int64_t *>(xs + (size_t)R * K);
+    int32_t *ccnt = reinterpret_cast<int32_t *>(cacc + 2 * G * B * N);
+    if (P > 1) {
+        for (int i = threadIdx.x; i < 2 * G * B * N; i += blockDim.x) cacc[i] = 0;
+        for (int i = threadIdx.x; i < 2 * G * B; i += blockDim.x) ccnt[i] = 0;
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = a.npairs * 2 / U;
     int u0, u1;
@@ -311,7 +324,7 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, (uint32_t)B);  // every warp of the owning group arrives
+            mbar_init(empty + s, (uint32_t)(B * P));  // every warp of the owning group arrives
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -364,7 +377,8 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
 
     // A parity wait is only unambiguous for the phase right after the one the
     // waiter consumed last, so each group waits on its own stage chunk by chunk.
-    const int grp = warp / B, slot = warp - grp * B;
+    const int grp = warp / (B * P), within = warp - grp * (B * P);
+    const int slot = within / P, part = within - slot * P;
     for (int j = grp; warp < C && j < nchunks; j += G) {
         const int s = j % S;
         if (!__all_sync(0xffffffffu, mbar_wait(full + s, (j / S) & 1))) {  // warp-uniform decision
@@ -374,14 +388,33 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
         const int jl = j * B + slot;  // local unit index
         int64_t acc[N];
         if (jl < nloc)
-            unit_dots<R, U, VPL>(reinterpret_cast<const uint4 *>(ring + (size_t)s * chunk_bytes + (size_t)slot * unit_bytes),
-                                 xs4, xr, KV8, lane, acc);
+            unit_dots<R, U, VPL, P>(
+                reinterpret_cast<const uint4 *>(ring + (size_t)s * chunk_bytes + (size_t)slot * unit_bytes), xs4, xr,
+                KV8, lane, part, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + s);  // this warp's part of the stage is free
         if (jl >= nloc) continue;
 
         int idx;
-        const int64_t tot = warp_reduce_n<N>(acc, lane, idx);
+        int64_t tot = warp_reduce_n<N>(acc, lane, idx);
+        if constexpr (P > 1) {
+            // Lock-free combine: no warp ever waits for another part.
+            const int cs = ((j / G) & 1) * G * B + grp * B + slot;
+            int64_t *cb = cacc + (size_t)cs * N;
+            if ((lane & (32 / N - 1)) == 0)
+                atomicAdd(reinterpret_cast<unsigned long long *>(cb + idx), (unsigned long long)tot);
+            __threadfence_block();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(ccnt + cs, 1) == P - 1;
+            if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+            __threadfence_block();
+            tot = *reinterpret_cast<volatile int64_t *>(cb + idx);
+            __syncwarp();
+            // reused two rounds later, after this warp has released the next chunk
+            if ((lane & (32 / N - 1)) == 0) cb[idx] = 0;
+            if (lane == 0) ccnt[cs] = 0;
+        }
         const int unit = u0 + jl;
         if (U == 2) {
             constexpr int kPartnerBit = 32 / N;
@@ -429,58 +462,73 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     }
 }
 
-size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk) {
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk, int parts) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
+    const size_t combine = parts > 1 ? (size_t)2 * stages * units_per_chunk * (U * rows_tmpl * 8 + 4) : 0;
     return 2 * kMaxStages * sizeof(uint64_t) + (size_t)stages * units_per_chunk * U * K * 2 +
-           (size_t)rows_tmpl * K * 2;
+           (size_t)rows_tmpl * K * 2 + combine;
 }
 
 // Ring plan.  1-D bulk copies only stream at full HBM rate when each copy is
 // large (>= 16 KiB on B200: 8 KiB copies cap near 4 TB/s), so a stage holds B
 // consecutive units making a ~32 KiB chunk, and G stages form the ring; the
-// consumer warps are G groups of B.  Limits: G*B <= consumer warps of the
-// kernel, G >= 2 (double buffering), shared memory within max_smem.
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk) {
+// consumer warps are G groups of B.  A unit of 16 KiB or more (the FFN-wide
+// Down rows) fills a stage alone and would leave one warp per stage to digest
+// it, so such units are split over P = 4 warps.  Limits: G*B*P <= consumer
+// warps of the kernel, G >= 2 (double buffering), shared memory within max_smem.
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const int unit = U * K * 2;
     const int cmax = rows_tmpl <= 2 ? 16 : 8;
     int B = (32 * 1024) / unit;
     if (B < 1) B = 1;
     if (B > cmax / 2) B = cmax / 2;
+    const int P = (U == 1 && B == 1 && unit >= 16 * 1024) ? 4 : 1;
     int G = ring_bytes / (B * unit);
-    if (G > cmax / B) G = cmax / B;
+    if (G > cmax / (B * P)) G = cmax / (B * P);
     if (G < 2) G = 2;
-    while (G > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B) > (size_t)max_smem) G--;
-    while (B > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B) > (size_t)max_smem) B--;
+    while (G > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B, P) > (size_t)max_smem) G--;
+    while (B > 1 && gemv_smem_bytes(rows_tmpl, epi, K, G, B, P) > (size_t)max_smem) B--;
     *units_per_chunk = B;
+    *parts = P;
     return G;
 }
 
-template <int R, int EPI, int VPL>
+template <int R, int EPI, int VPL, int P>
 static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     ProjArgs c = a;
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3((a.stages * a.units_per_chunk + 1) * 32);  // consumer groups + producer
-    cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages, a.units_per_chunk);
+    cfg.blockDim = dim3((a.stages * a.units_per_chunk * P + 1) * 32);  // consumer groups + producer
+    cfg.dynamicSmemBytes = gemv_smem_bytes(R, EPI, a.K, a.stages, a.units_per_chunk, P);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI, VPL>, args);
+    return cudaLaunchKernelExC(&cfg, (const void *)k_gemv<R, EPI, VPL, P>, args);
 }
 
 // Fully unrolled paths for the Qwen2.5-3B input widths: K = 2048 (hidden) and
 // K = 11008 (FFN, single GPU); everything else takes the generic loop.
+// Units split over 4 warps exist only for the one-row-per-unit epilogues.
 template <int R, int EPI>
 static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
-    if (a.K == 2048) return launch_gemv_v<R, EPI, 8>(a, grid, st);
-    if (R <= 2 && (EPI == EPI_RESID || EPI == EPI_PARTIAL) && a.K == 11008)
-        return launch_gemv_v<R, EPI, 43>(a, grid, st);
-    return launch_gemv_v<R, EPI, 0>(a, grid, st);
+    constexpr bool kSplit = EPI == EPI_RESID || EPI == EPI_PARTIAL;
+    if constexpr (kSplit) {
+        if (a.parts == 4) {
+            if constexpr (R <= 2)
+                if (a.K == 11008) return launch_gemv_v<R, EPI, 43, 4>(a, grid, st);
+            return launch_gemv_v<R, EPI, 0, 4>(a, grid, st);
+        }
+        if constexpr (R <= 2)
+            if (a.K == 11008 && a.parts == 1) return launch_gemv_v<R, EPI, 43, 1>(a, grid, st);
+    }
+    if (a.parts != 1) return cudaErrorInvalidValue;
+    if (a.K == 2048) return launch_gemv_v<R, EPI, 8, 1>(a, grid, st);
+    return launch_gemv_v<R, EPI, 0, 1>(a, grid, st);
 }
 
 template <int EPI>
@@ -504,13 +552,17 @@ cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cud
 
 template <int R, int EPI>
 static cudaError_t configure_r(int bytes) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    constexpr auto kAttr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8, 1>, kAttr, bytes);
     if (e) return e;
-    if (R <= 2 && (EPI == EPI_RESID || EPI == EPI_PARTIAL)) {
-        e = cudaFuncSetAttribute(k_gemv<R, EPI, 43>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-        if (e) return e;
+    if constexpr (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
+        if (R <= 2) {
+            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 1>, kAttr, bytes))) return e;
+            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 4>, kAttr, bytes))) return e;
+        }
+        if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 0, 4>, kAttr, bytes))) return e;
     }
-    return cudaFuncSetAttribute(k_gemv<R, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return cudaFuncSetAttribute(k_gemv<R, EPI, 0, 1>, kAttr, bytes);
 }
 
 template <int EPI>

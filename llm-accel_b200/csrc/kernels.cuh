@@ -1,6 +1,7 @@
 // Kernel argument blocks and launch entry points of the resident layer path.
 #pragma once
 #include <cuda_runtime.h>
+
 #include <cstdint>
 
 namespace llmx {
@@ -45,7 +46,8 @@ struct ProjArgs {
     int kv_pairs;        // pairs of K (= of V) (kv_heads * hd/2)
     int max_seq;
     int stages;          // shared-memory ring stages G (gemv_stages)
-    int units_per_chunk; // units B per stage / bulk copy; G*B consumer warps
+    int units_per_chunk; // units B per stage / bulk copy
+    int parts;           // warps sharing one unit along K (1 or 4); G*B*parts consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
 };
 
@@ -94,8 +96,8 @@ size_t attn_smem_bytes(int tpc, int hd);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 cudaError_t proj_configure(int max_smem_bytes);
-size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk);
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk);
+size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk, int parts);
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts);
 
 // Weight layout kernel (model upload): slot s of the destination receives
 // dense row row_of_slot[s], columns [col0, col0+K), as K/2 32-bit words; word j

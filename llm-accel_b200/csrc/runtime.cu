@@ -122,7 +122,7 @@ int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
 
 void set_stages(llmx_ctx *c, ProjArgs &a, int epi, int rt) {
     const int smem = kProjSmem / c->gemv_ctas_per_sm - 1024;
-    a.stages = gemv_stages(rt, epi, a.K, smem, c->ring_kb * 1024, &a.units_per_chunk);
+    a.stages = gemv_stages(rt, epi, a.K, smem, c->ring_kb * 1024, &a.units_per_chunk, &a.parts);
     a.error = c->err;
 }
 
