@@ -230,6 +230,32 @@ int llmx_time_kernel(llmx_ctx *ctx, int kernel, uint32_t layer, uint32_t positio
                      uint32_t rows, int iters, double *ms_per_launch);
 
 /* ---------------------------------------------------------------------------
+ * LM-head argmax on the device, without allocation.  No counterpart in the
+ * reference: its argmax runs on the host (model_data_t::lm_head_argmax
+ * host:937-977), which llmx_model_lm_head_argmax mirrors; this returns the
+ * same tokens (exact int64 scores, the first maximum wins).
+ *
+ * For callers that cannot allocate device memory at sampling time: a serving
+ * loop whose HBM is fully committed to weights and KV cache, or code running
+ * several streams where cudaMalloc / cudaFree would synchronise the device.
+ * The call allocates nothing; its scratch is one fixed 128 KiB device array
+ * per device (8 rows x 1024 blocks of partial results), shared by every call.
+ *
+ *   hidden   device, [rows][hidden_size] int16 (Q8.8), 16-byte aligned
+ *   lm_head  device, [vocab][hidden_size] int16 (Q4.12), 16-byte aligned
+ *   tokens   device, [rows] uint32 (written in stream order)
+ *   stream   cudaStream_t as void* (NULL = legacy default stream)
+ * Limits: 1 <= rows <= 8 (LLMX_ERR_ARG beyond), hidden_size a multiple of 8.
+ * The first call on each device does a one-time set-up there (looks up the
+ * scratch array's address); make that first call before any stream capture.
+ * Calls share the scratch, so calls that may overlap on the device (different
+ * streams without ordering) race: order them on one stream or with events.
+ * Stream-ordered: returns after enqueueing two kernels. */
+int llmx_lm_head_argmax_device(const int16_t *hidden, uint32_t rows, uint32_t hidden_size,
+                               const int16_t *lm_head, uint32_t vocab, uint32_t *tokens,
+                               void *stream);
+
+/* ---------------------------------------------------------------------------
  * Host runtime: qwen_executor_t host:7607-8161
  * ------------------------------------------------------------------------- */
 /* run_prompt_block host:7840-7918: embedding rows of 1..8 tokens at

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <string>
 #include <cstdint>
 
 namespace llmx {
@@ -107,5 +108,8 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
 cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
                               const int32_t *row_of_slot, int nslots, uint32_t *dst,
                               cudaStream_t s);
+
+// Message returned by llmx_last_error() on this thread.
+void set_last_error(const std::string &msg);
 
 }  // namespace llmx

@@ -1,0 +1,226 @@
+// LM-head argmax on the GPU for callers that must not allocate device memory.
+//
+// The host path (model_data_t::lm_head_argmax, host/host_qwen_8x64.cpp:937-977)
+// scores every vocabulary row with an exact int64 dot product against one
+// final-normed hidden row and keeps the first maximum.  This file computes the
+// same tokens on the device.  It is meant for callers that cannot allocate at
+// the point where they sample: a serving loop whose HBM is already committed
+// in full to weights and KV cache (an allocation there fails or evicts), and
+// code that runs between tokens on several streams, where cudaMalloc/cudaFree
+// would serialise the whole device.  So the entry point allocates nothing.
+// Its per-block partial results live in one file-scope device array; every
+// call on a device shares that array.
+//
+// Kernels: k_lm_scan (one pass over the LM head; each block keeps the best
+// (score, token) per row of its contiguous vocabulary range) and k_lm_pick
+// (one block reduces the block results in vocabulary order).
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/llmx.h"
+#include "device_util.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+constexpr int kPickRows = 8;           // rows per call (the controller's block size)
+constexpr int kScanBlocks = 1024;      // upper bound of the scan grid
+constexpr int kScanThreads = 256;
+constexpr int kMaxDevices = 64;
+
+struct Best {
+    long long score;
+    unsigned int token;
+    unsigned int pad;
+};
+
+// Scratch: Best[row][block], 8 x 1024 x 16 B = 128 KiB per device.  Every slot
+// that k_lm_pick reads is written by k_lm_scan earlier in the same call, so
+// nothing in it has to start at zero and nothing is cleared between calls.
+static __device__ __align__(256) Best g_pick_scratch[kPickRows * kScanBlocks];
+
+// Better = higher score; among equal scores the lower token (the first
+// maximum of a scan in vocabulary order).
+static __device__ __forceinline__ bool better(long long s, unsigned t, long long bs, unsigned bt) {
+    return s > bs || (s == bs && t < bt);
+}
+
+static __device__ __forceinline__ long long dot8(uint4 h, uint4 w) {
+    const uint32_t hv[4] = {h.x, h.y, h.z, h.w}, wv[4] = {w.x, w.y, w.z, w.w};
+    long long s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        s += (long long)(int32_t)llmx::lo16(hv[k]) * (int32_t)llmx::lo16(wv[k]);
+        s += (long long)(int32_t)llmx::hi16(hv[k]) * (int32_t)llmx::hi16(wv[k]);
+    }
+    return s;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kScanThreads) k_lm_scan(const int16_t *__restrict__ h, int hidden,
+                                                          const int16_t *__restrict__ w, unsigned vocab,
+                                                          int rows, Best *__restrict__ part) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const unsigned v0 = (unsigned)((unsigned long long)vocab * blockIdx.x / gridDim.x);
+    const unsigned v1 = (unsigned)((unsigned long long)vocab * (blockIdx.x + 1) / gridDim.x);
+    const int nvec = hidden >> 3;
+    const uint4 *h4 = reinterpret_cast<const uint4 *>(h);
+    long long best[R];
+    unsigned arg[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        best[r] = LLONG_MIN;
+        arg[r] = 0xffffffffu;
+    }
+    for (unsigned v = v0 + warp; v < v1; v += nw) {
+        const uint4 *wr = reinterpret_cast<const uint4 *>(w + (size_t)v * hidden);
+        long long acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = 0;
+#pragma unroll 8
+        for (int k = lane; k < nvec; k += 32) {
+            const uint4 wv = llmx::ld_stream(wr + k);
+#pragma unroll
+            for (int r = 0; r < R; r++)
+                if (r < rows) acc[r] += dot8(__ldg(h4 + (size_t)r * nvec + k), wv);
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) acc[r] += llmx::shfl_xor64(acc[r], o);
+            if (acc[r] > best[r]) {  // this warp visits its tokens in increasing order
+                best[r] = acc[r];
+                arg[r] = v;
+            }
+        }
+    }
+    __shared__ long long sb[kScanThreads / 32][R];
+    __shared__ unsigned st[kScanThreads / 32][R];
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            sb[warp][r] = best[r];
+            st[warp][r] = arg[r];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < rows) {
+        const int r = threadIdx.x;
+        long long bs = LLONG_MIN;
+        unsigned bt = 0xffffffffu;
+        for (int q = 0; q < nw; q++)
+            if (st[q][r] != 0xffffffffu && better(sb[q][r], st[q][r], bs, bt)) {
+                bs = sb[q][r];
+                bt = st[q][r];
+            }
+        part[(size_t)r * kScanBlocks + blockIdx.x] = Best{bs, bt, 0u};
+    }
+}
+
+__global__ void __launch_bounds__(kPickRows * 32) k_lm_pick(const Best *__restrict__ part, int nblocks, int rows,
+                                                           uint32_t *__restrict__ tokens) {
+    const int r = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    long long bs = LLONG_MIN;
+    unsigned bt = 0xffffffffu;
+    for (int b = lane; b < nblocks; b += 32) {
+        const Best p = part[(size_t)r * kScanBlocks + b];
+        if (p.token != 0xffffffffu && better(p.score, p.token, bs, bt)) {
+            bs = p.score;
+            bt = p.token;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const long long os = llmx::shfl_xor64(bs, o);
+        const unsigned ot = __shfl_xor_sync(0xffffffffu, bt, o);
+        if (ot != 0xffffffffu && (bt == 0xffffffffu || better(os, ot, bs, bt))) {
+            bs = os;
+            bt = ot;
+        }
+    }
+    if (lane == 0) tokens[r] = bt;
+}
+
+// Per-device set-up: the scratch array's device address and the SM count,
+// looked up once with that device current.
+struct DeviceSetup {
+    bool ready = false;
+    Best *scratch = nullptr;
+    int nsm = 0;
+};
+std::mutex g_setup_mu;
+DeviceSetup g_setup[kMaxDevices];
+
+int fail(int code, const std::string &msg) {
+    llmx::set_last_error(msg);
+    return code;
+}
+
+template <int R>
+cudaError_t launch_scan(const int16_t *h, int hidden, const int16_t *w, unsigned vocab, int rows, Best *part,
+                        int grid, cudaStream_t s) {
+    k_lm_scan<R><<<grid, kScanThreads, 0, s>>>(h, hidden, w, vocab, rows, part);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int llmx_lm_head_argmax_device(const int16_t *hidden, uint32_t rows, uint32_t hidden_size,
+                                          const int16_t *lm_head, uint32_t vocab, uint32_t *tokens,
+                                          void *stream) {
+    if (!hidden || !lm_head || !tokens) return fail(LLMX_ERR_ARG, "lm_head_argmax_device: null pointer");
+    if (rows == 0 || rows > (uint32_t)kPickRows)
+        return fail(LLMX_ERR_ARG, "lm_head_argmax_device: rows must be 1..8 (the scratch array holds 8 rows), got " +
+                                      std::to_string(rows));
+    if (hidden_size == 0 || hidden_size % 8 != 0 || hidden_size > (1u << 20))
+        return fail(LLMX_ERR_ARG, "lm_head_argmax_device: hidden_size must be a positive multiple of 8 up to 2^20");
+    if (vocab == 0 || vocab > (uint32_t)INT_MAX)
+        return fail(LLMX_ERR_ARG, "lm_head_argmax_device: vocab must be 1..2^31-1");
+    if (((uintptr_t)hidden | (uintptr_t)lm_head) & 15u)
+        return fail(LLMX_ERR_ARG, "lm_head_argmax_device: hidden and lm_head must be 16-byte aligned");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(LLMX_ERR_UNSUPPORTED, "lm_head_argmax_device: device ordinal >= 64");
+    DeviceSetup su;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mu);
+        if (!g_setup[dev].ready) {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_pick_scratch);
+            if (e != cudaSuccess)
+                return fail(LLMX_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+            int nsm = 0;
+            e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess)
+                return fail(LLMX_ERR_CUDA, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+            g_setup[dev].scratch = static_cast<Best *>(p);
+            g_setup[dev].nsm = nsm;
+            g_setup[dev].ready = true;
+        }
+        su = g_setup[dev];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // 4 blocks of 8 warps per SM keep enough 16-byte loads in flight to stream the
+    // table at HBM rate; never more blocks than the scratch holds or than rows.
+    long long grid = (long long)su.nsm * 4;
+    if (grid > kScanBlocks) grid = kScanBlocks;
+    if (grid > (long long)vocab) grid = vocab;
+    const int R = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;
+    switch (R) {
+    case 1: e = launch_scan<1>(hidden, (int)hidden_size, lm_head, vocab, (int)rows, su.scratch, (int)grid, s); break;
+    case 2: e = launch_scan<2>(hidden, (int)hidden_size, lm_head, vocab, (int)rows, su.scratch, (int)grid, s); break;
+    case 4: e = launch_scan<4>(hidden, (int)hidden_size, lm_head, vocab, (int)rows, su.scratch, (int)grid, s); break;
+    default: e = launch_scan<8>(hidden, (int)hidden_size, lm_head, vocab, (int)rows, su.scratch, (int)grid, s); break;
+    }
+    if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("k_lm_scan: ") + cudaGetErrorString(e));
+    k_lm_pick<<<1, kPickRows * 32, 0, s>>>(su.scratch, (int)grid, (int)rows, tokens);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(LLMX_ERR_CUDA, std::string("k_lm_pick: ") + cudaGetErrorString(e));
+    return LLMX_OK;
+}

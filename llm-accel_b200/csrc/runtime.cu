@@ -55,6 +55,8 @@ int rows_template(uint32_t rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <
 
 }  // namespace
 
+void llmx::set_last_error(const std::string &msg) { g_last_error = msg; }
+
 struct llmx_ctx {
     llmx_shape s{};
     int dev = 0, rank = 0, size = 1, nsm = 148;

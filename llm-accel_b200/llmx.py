@@ -121,6 +121,7 @@ def lib():
                                            C.POINTER(C.c_double)]),
             "llmx_run_prompt_block": (C.c_int, [vp, vp, u32p, C.c_uint32, C.c_uint32, C.c_int, i16p]),
             "llmx_run_token": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, i16p]),
+            "llmx_lm_head_argmax_device": (C.c_int, [vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -234,6 +235,13 @@ class Model:
         check(lib().llmx_model_lm_head_argmax(self.h, np.ascontiguousarray(hidden_row, np.int16).reshape(-1),
                                               threads, C.byref(tok)), "lm_head_argmax")
         return tok.value
+
+
+def lm_head_argmax_device(hidden_ptr, rows, hidden_size, lm_head_ptr, vocab, tokens_ptr, stream=None):
+    """llmx_lm_head_argmax_device on device pointers (ints); allocates nothing.
+    Returns the status code without raising."""
+    return lib().llmx_lm_head_argmax_device(hidden_ptr, rows, hidden_size, lm_head_ptr, vocab, tokens_ptr,
+                                            stream)
 
 
 def tp_unique_id() -> bytes:
