@@ -86,12 +86,6 @@ size_t attn_smem_bytes(int tpc, int hd) {
     return attn_layout(tpc, hd, off);
 }
 
-// floor(2^32 / s) for 16 <= s < 2^31 (the quotient of accum(1) / safe_sum,
-// host:3727-3730: (1.0 << 16) / s with 16 fraction bits, truncated)
-static __device__ __forceinline__ uint32_t recip_q16(int32_t s) {
-    const uint32_t u = (uint32_t)s;
-    return 0xffffffffu / u + ((u & (u - 1)) == 0 ? 1u : 0u);
-}
 
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     extern __shared__ __align__(16) char raw[];

@@ -82,4 +82,11 @@ __host__ __device__ inline int32_t inv_rms_q88(int32_t sum_sq, int32_t inv_elems
 }
 __host__ __device__ inline int32_t fm_from_count(int n) { return n >= 128 ? 32767 : n * 256; }
 
+// floor(2^32 / s) for 16 <= s < 2^31 (the quotient of accum(1) / safe_sum,
+// host:3727-3730: (1.0 << 16) / s with 16 fraction bits, truncated)
+__host__ __device__ __forceinline__ uint32_t recip_q16(int32_t s) {
+    const uint32_t u = (uint32_t)s;
+    return 0xffffffffu / u + ((u & (u - 1)) == 0 ? 1u : 0u);
+}
+
 }  // namespace llmx

@@ -26,6 +26,7 @@
 #include "device_util.cuh"
 #include "fixed.cuh"
 #include "kernels.cuh"
+#include "gemv_common.cuh"
 
 namespace llmx {
 
@@ -36,88 +37,6 @@ struct Warps {
     static constexpr int kConsumers = R <= 2 ? 16 : 8;
     static constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
 };
-constexpr int kMaxStages = 32;
-constexpr uint32_t kSpinLimit = 1u << 26;           // bounded mbarrier waits (seconds of polling)
-
-// ---- mbarrier / bulk-copy primitives ---------------------------------------
-static __device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-static __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-static __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-static __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-static __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait: false when the limit expired (the caller records an error).
-static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kSpinLimit; i++)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-static __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-// Named barrier over the consumer warps (the producer warp is the last warp).
-static __device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 32) : "memory");
-}
-
-// golden_silu host:658-668 / cu_silu_approx kernel/compute_stream.cpp:88-96,
-// then x up with one rounding (stream_silu_mul :123-164).
-static __device__ __forceinline__ int32_t silu_mul(int32_t g, int32_t u, const int16_t *__restrict__ etab) {
-    int32_t s;
-    if (g >= 0) {
-        const int32_t e = __ldg(etab + (g > 2048 ? 0 : 2048 - g));
-        const int32_t r = recip_q88(sat16(256 + e));
-        s = sat16(rnd((int64_t)g * r, 8));
-    } else {
-        const int32_t e = __ldg(etab + (g < -2048 ? 0 : g + 2048));
-        const int32_t r = recip_q88(sat16(256 + e));
-        s = sat16(rnd((int64_t)g * e * r, 16));
-    }
-    return sat16(rnd((int64_t)s * u, 8));
-}
-
-// Halving ("transpose") warp reduction of N int64 values: afterwards lane L
-// holds the warp total of value index idx(L); lanes that differ only in the
-// bits below 32/N hold the same index.  N <= 16.
-template <int N>
-static __device__ __forceinline__ int64_t warp_reduce_n(int64_t (&v)[N], int lane, int &idx) {
-    idx = 0;
-#pragma unroll
-    for (int n = N, o = 16; n > 1; n >>= 1, o >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < n / 2; i++) {
-            const int64_t send = up ? v[i] : v[i + n / 2];
-            const int64_t keep = up ? v[i + n / 2] : v[i];
-            v[i] = keep + shfl_xor64(send, o);
-        }
-        if (up) idx += n / 2;
-    }
-    int64_t t = v[0];
-#pragma unroll
-    for (int o = 16 / N; o >= 1; o >>= 1) t += shfl_xor64(t, o);
-    return t;
-}
-
 // Activation prologue (consumer warps): rows -> shared memory, RMS-normalised
 // when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
 template <int R>
@@ -198,95 +117,6 @@ static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) 
     u1 = (int)((int64_t)nunits * (blockIdx.x + 1) / gridDim.x);
 }
 
-// One unit's dot products against R activation rows, accumulated exactly.
-// VPL > 0: K == 256 * VPL, every lane takes VPL 16-byte vectors per row (fully
-// unrolled, no predicates; K = 2048 -> 8, K = 11008 -> 43); VPL == 0: any K,
-// 16-vector chunks.  The int32 partials are flushed to int64 every 16 vectors:
-//   |lo| <= 16*8*255*32768 < 2^30, |hi| <= 16*8*128*32768 = 2^29 per flush.
-// P > 1: the unit is shared by P warps; warp `part` takes every P-th group of
-// 32 vectors, and the P partial sums are added afterwards (exact int64).
-template <int R, int U, int VPL, int P>
-static __device__ __forceinline__ void unit_dots(const uint4 *__restrict__ wv, const uint4 *__restrict__ xs4,
-                                                 const uint4 (&xr)[8], int KV8, int lane, int part,
-                                                 int64_t (&acc)[U * R]) {
-    constexpr int N = U * R;
-#pragma unroll
-    for (int i = 0; i < N; i++) acc[i] = 0;
-    if constexpr (VPL > 0) {
-        int lo[N], hi[N];
-#pragma unroll
-        for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
-        constexpr int KI = ((VPL > 0 ? VPL : 1) + P - 1) / P;  // vector groups of this warp
-#pragma unroll
-        for (int ki = 0; ki < KI; ki++) {
-            const int k = P == 1 ? ki : ki * P + part;
-            if (P > 1 && ki == KI - 1 && k >= VPL) break;
-            if (ki > 0 && ki % 16 == 0) {  // flush the int32 partials every 16 vectors
-#pragma unroll
-                for (int i = 0; i < N; i++) {
-                    acc[i] += (int64_t)hi[i] * 256 + lo[i];
-                    lo[i] = hi[i] = 0;
-                }
-            }
-            const int v = k * 32 + lane;
-            uint4 w[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const uint4 x = (R == 1 && VPL <= 8 && P == 1) ? xr[k < 8 ? k : 0] : xs4[r * KV8 + v];
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    const int i = r * U + u;
-                    lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
-                    hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
-                    lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
-                    hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
-                    lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
-                    hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
-                    lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
-                    hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
-    } else {
-    for (int v0 = part * 32; v0 < KV8; v0 += 16 * 32 * P) {
-        int lo[N], hi[N];
-#pragma unroll
-        for (int i = 0; i < N; i++) lo[i] = hi[i] = 0;
-#pragma unroll 4
-        for (int k = 0; k < 16; k++) {
-            const int v = v0 + k * 32 * P + lane;
-            if (v < KV8) {
-                uint4 w[U];
-#pragma unroll
-                for (int u = 0; u < U; u++) w[u] = wv[u * KV8 + v];
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    const uint4 x = xs4[r * KV8 + v];
-#pragma unroll
-                    for (int u = 0; u < U; u++) {
-                        const int i = r * U + u;
-                        lo[i] = dp2a_lo_su(x.x, w[u].x, lo[i]);
-                        hi[i] = dp2a_hi_ss(x.x, w[u].x, hi[i]);
-                        lo[i] = dp2a_lo_su(x.y, w[u].y, lo[i]);
-                        hi[i] = dp2a_hi_ss(x.y, w[u].y, hi[i]);
-                        lo[i] = dp2a_lo_su(x.z, w[u].z, lo[i]);
-                        hi[i] = dp2a_hi_ss(x.z, w[u].z, hi[i]);
-                        lo[i] = dp2a_lo_su(x.w, w[u].w, lo[i]);
-                        hi[i] = dp2a_hi_ss(x.w, w[u].w, hi[i]);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < N; i++) acc[i] += (int64_t)hi[i] * 256 + lo[i];
-    }
-    }
-}
-
 template <int R, int EPI, int VPL, int P>
 __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a) {
     constexpr int U = GemvTraits<R, EPI>::U;
@@ -332,6 +162,7 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
 
     if (warp == (int)(blockDim.x >> 5) - 1) {  // ---------------- producer warp -------------
         if (lane == 0) {
+            const uint64_t policy = evict_first_policy();  // weights are read once per step
             const char *src = reinterpret_cast<const char *>(a.w) + (size_t)u0 * unit_bytes;
             bool ok = true;
             int issued = 0;
@@ -343,7 +174,7 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
                 }
                 const uint32_t bytes = (uint32_t)min(B, nloc - j * B) * unit_bytes;
                 mbar_expect_tx(full + s, bytes);
-                bulk_g2s(ring + (size_t)s * chunk_bytes, src + (size_t)j * chunk_bytes, bytes, full + s);
+                bulk_g2s_hint(ring + (size_t)s * chunk_bytes, src + (size_t)j * chunk_bytes, bytes, full + s, policy);
                 issued = j + 1;
                 if (j == S - 1) pdl_wait();  // ring primed before waiting on the producer kernel
             }

@@ -4,7 +4,7 @@
 #include <cstdint>
 #include <vector>
 
-#include "../../include/llmx.h"
+#include "llmx.h"
 
 struct llmx_model {
     llmx_shape shape{};

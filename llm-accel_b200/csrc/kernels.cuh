@@ -109,6 +109,35 @@ cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
                               const int32_t *row_of_slot, int nslots, uint32_t *dst,
                               cudaStream_t s);
 
+// Fused one-row decode of a whole layer stack (stack.cu): one persistent
+// cooperative kernel, phases separated by bounded grid barriers.
+struct StackArgs {
+    const uint32_t *wbuf;      // packed weights of all layers
+    size_t layer_words;        // words per layer
+    size_t off_o, off_gu, off_d; // word offsets of O, Gate/Up, Down within a layer
+    int H, Hq, KV, Il, hd, heads, gqa, max_seq;
+    int layer_begin, layer_count, final_norm;
+    const int16_t *norms, *rope, *etab, *ptab;
+    int16_t *kc, *vc;          // layer-0 caches; one layer = kv_heads*max_seq*hd further
+    int16_t *hid0, *hid1, *q, *att, *act;
+    int16_t *sc;               // [heads][max_seq] attention scores
+    int32_t *tmax;             // [heads][kStackMaxTiles] tile maxima
+    unsigned *bar;             // grid barrier counter, zero at launch
+    int *error;
+    const Step *step;
+    int32_t inv_elems, inv_rms_const, qk_scale;
+    int b_qkv, b_o, b_gu, b_d; // max units per ring chunk, per phase
+    int p_d;                   // warps sharing one Down unit (1, 2 or 4)
+    int x_bytes;               // activation / attention scratch bytes in shared memory
+    const int16_t *norm_final; // Task 20 norm row
+};
+constexpr int kStackMaxTiles = 40;  // max_seq <= 2560
+// Plan the fused kernel for a shape; false when the shape does not fit it.
+bool stack_plan(int H, int Hq, int KV, int Il, int hd, int max_seq, int nsm, StackArgs &a, size_t &smem);
+cudaError_t stack_configure(size_t smem);
+cudaError_t launch_stack(const StackArgs &a, size_t smem, int grid, cudaStream_t s);
+int stack_threads();
+
 // Message returned by llmx_last_error() on this thread.
 void set_last_error(const std::string &msg);
 

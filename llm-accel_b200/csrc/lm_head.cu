@@ -21,7 +21,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/llmx.h"
+#include "llmx.h"
 #include "device_util.cuh"
 #include "kernels.cuh"
 

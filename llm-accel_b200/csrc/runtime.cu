@@ -45,10 +45,11 @@ int fail_cuda(cudaError_t e, const char *what) {
         }                                                                     \
     } while (0)
 
-__global__ void k_set_step(Step *dst, int32_t position, int32_t rows) {
+__global__ void k_set_step(Step *dst, int32_t position, int32_t rows, unsigned *bar) {
     asm volatile("griddepcontrol.launch_dependents;");
     dst->position = position;
     dst->rows = rows;
+    if (bar) *bar = 0u;  // grid barrier counter of the fused decode kernel
 }
 
 int rows_template(uint32_t rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8; }
@@ -77,6 +78,13 @@ struct llmx_ctx {
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, gemv_ctas_per_sm = 1;
+    // fused one-row decode (stack.cu): plan, scratch, barrier counter
+    bool fused = false;
+    StackArgs stack{};
+    size_t stack_smem = 0;
+    int16_t *sc = nullptr;
+    int32_t *tmax = nullptr;
+    unsigned *bar = nullptr;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -273,7 +281,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
 }
 
 int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
-    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows);
+    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows, c->bar);
     CK(cudaGetLastError());
     c->launches += 1;
     return LLMX_OK;
@@ -333,6 +341,19 @@ int launch_stack_graph(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_
     }
     CK(cudaGraphLaunch(it->second.first, c->stream));
     c->launches += it->second.second;
+    return LLMX_OK;
+}
+
+// One-row stacks on one GPU run as a single cooperative kernel (stack.cu).
+bool use_fused(const llmx_ctx *c, uint32_t rows) { return c->fused && rows == 1; }
+
+int launch_fused(llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count, int final_norm) {
+    StackArgs a = c->stack;
+    a.layer_begin = (int)layer_begin;
+    a.layer_count = (int)layer_count;
+    a.final_norm = final_norm;
+    CK(launch_stack(a, c->stack_smem, c->nsm, c->stream));
+    c->launches += 1;
     return LLMX_OK;
 }
 
@@ -471,6 +492,57 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         c->inv_elems = recip_q88(fm_from_count(s.hidden));
         c->inv_rms_const = inv_rms_q88(0, 0);
         c->qk_scale = qk_scale_q1616(hd);
+    }
+    // fused one-row decode (opt-in, LLMX_FUSED_DECODE=1): one GPU, a shape the
+    // kernel's plan accepts, and a cooperative launch of one CTA per SM
+    if (tp_size == 1 && env_int("LLMX_FUSED_DECODE", 0, 0, 1) == 1) {
+        StackArgs &a = c->stack;
+        size_t smem = 0;
+        int coop = 0;
+        e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "cudaDeviceGetAttribute"));
+        if (coop && stack_plan(s.hidden, c->Hq, c->KV, c->Il, hd, s.max_seq, c->nsm, a, smem) &&
+            stack_configure(smem) == cudaSuccess) {
+            if ((rc = dalloc(c, &c->sc, (size_t)s.heads * s.max_seq)) ||
+                (rc = dalloc(c, &c->tmax, (size_t)s.heads * kStackMaxTiles)) || (rc = dalloc(c, &c->bar, 1)))
+                return bail(rc);
+            a.wbuf = c->wbuf;
+            a.layer_words = c->layer_words;
+            a.off_o = c->w_qkv;
+            a.off_gu = c->w_qkv + c->w_o;
+            a.off_d = c->w_qkv + c->w_o + c->w_gu;
+            a.H = s.hidden;
+            a.Hq = c->Hq;
+            a.KV = c->KV;
+            a.Il = c->Il;
+            a.hd = hd;
+            a.heads = s.heads;
+            a.gqa = G;
+            a.max_seq = s.max_seq;
+            a.norms = c->norms;
+            a.norm_final = c->norms + (size_t)2 * s.layers * s.hidden;
+            a.rope = c->rope;
+            a.etab = c->etab;
+            a.ptab = c->ptab;
+            a.kc = c->kc;
+            a.vc = c->vc;
+            a.hid0 = c->hid[0];
+            a.hid1 = c->hid[1];
+            a.q = c->q;
+            a.att = c->att;
+            a.act = c->act;
+            a.sc = c->sc;
+            a.tmax = c->tmax;
+            a.bar = c->bar;
+            a.error = c->err;
+            a.step = c->step;
+            a.inv_elems = c->inv_elems;
+            a.inv_rms_const = c->inv_rms_const;
+            a.qk_scale = c->qk_scale;
+            c->stack_smem = smem;
+            c->fused = true;
+        }
+        cudaGetLastError();  // a refused smem opt-in only disables the fused path
     }
     if (tp_size > 1) {
         ncclUniqueId id;
@@ -627,7 +699,10 @@ int llmx_stack_async(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t 
     CK(cudaSetDevice(c->dev));
     const uint64_t before = c->launches;
     int rc = set_step(c, position, rows);
-    if (!rc) rc = launch_stack_graph(c, rows, layer_begin, layer_count, include_final_norm ? 1 : 0);
+    if (!rc && use_fused(c, rows))
+        rc = launch_fused(c, layer_begin, layer_count, include_final_norm ? 1 : 0);
+    else if (!rc)
+        rc = launch_stack_graph(c, rows, layer_begin, layer_count, include_final_norm ? 1 : 0);
     c->last_launches = c->launches - before;
     return rc;
 }
