@@ -39,6 +39,8 @@ struct Warps {
 };
 // Activation prologue (consumer warps): rows -> shared memory, RMS-normalised
 // when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
+constexpr int kStageBatch = 4;  // 16-byte activation loads in flight per thread while staging
+
 template <int R>
 static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int tid) {
     constexpr int CW = Warps<R>::kConsumers;  // upper bound of the consumer warps
@@ -80,28 +82,50 @@ static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int 
         consumer_sync();
         const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
         const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm);
-        for (int i = tid; i < R * KV8; i += T) {
-            const int r = i / KV8, v = i - r * KV8;
-            uint4 o = make_uint4(0, 0, 0, 0);
-            if (r < rows) {
-                const uint4 xv = x4[(size_t)r * KV8 + v], wv = w4[v];
-                const int64_t inv = inv_rms_s[r];
-                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        // all loads of a batch in flight before any is used (one L2 round trip per batch)
+        for (int i0 = tid; i0 < R * KV8; i0 += kStageBatch * T) {
+            uint4 xv[kStageBatch], wv[kStageBatch];
+#pragma unroll
+            for (int k = 0; k < kStageBatch; k++) {
+                const int i = i0 + k * T, r = i / KV8, v = i - r * KV8;
+                xv[k] = wv[k] = make_uint4(0, 0, 0, 0);
+                if (i < R * KV8 && r < rows) {
+                    xv[k] = x4[(size_t)r * KV8 + v];
+                    wv[k] = w4[v];
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kStageBatch; k++) {
+                const int i = i0 + k * T, r = i / KV8;
+                if (i >= R * KV8) break;
+                const int64_t inv = r < rows ? inv_rms_s[r] : 0;
+                const uint32_t xw[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+                const uint32_t ww[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
                 uint32_t ow[4];
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int32_t y0 = sat16(rnd((int64_t)lo16(xw[k]) * inv * lo16(ww[k]), 16));
-                    const int32_t y1 = sat16(rnd((int64_t)hi16(xw[k]) * inv * hi16(ww[k]), 16));
-                    ow[k] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+                for (int q = 0; q < 4; q++) {
+                    const int32_t y0 = sat16(rnd((int64_t)lo16(xw[q]) * inv * lo16(ww[q]), 16));
+                    const int32_t y1 = sat16(rnd((int64_t)hi16(xw[q]) * inv * hi16(ww[q]), 16));
+                    ow[q] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
                 }
-                o = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+                reinterpret_cast<uint4 *>(xs)[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
             }
-            reinterpret_cast<uint4 *>(xs)[i] = o;
         }
     } else {
         const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x);
-        for (int i = tid; i < R * KV8; i += T)
-            reinterpret_cast<uint4 *>(xs)[i] = (i / KV8) < rows ? x4[i] : make_uint4(0, 0, 0, 0);
+        for (int i0 = tid; i0 < R * KV8; i0 += kStageBatch * T) {
+            uint4 xv[kStageBatch];
+#pragma unroll
+            for (int k = 0; k < kStageBatch; k++) {
+                const int i = i0 + k * T;
+                xv[k] = (i < R * KV8 && i / KV8 < rows) ? x4[i] : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int k = 0; k < kStageBatch; k++) {
+                const int i = i0 + k * T;
+                if (i < R * KV8) reinterpret_cast<uint4 *>(xs)[i] = xv[k];
+            }
+        }
     }
     consumer_sync();
 }
