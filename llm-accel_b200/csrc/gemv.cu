@@ -221,6 +221,9 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     pdl_trigger();
     const Step st = *a.step;
     const int rows = st.rows;
+    const int ar_epoch = (EPI == EPI_PARTIAL && a.ar.n > 1) ? *a.ar.epoch : 0;
+    const int ar_slot = ar_epoch & 1;
+    const uint32_t ar_tag = (uint32_t)ar_epoch + 1u;
     stage_rows<R>(a, xs, rows, tid);
     const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
     uint4 xr[8];  // 1-row decode with K <= 2048: this lane's activation vectors stay in registers
@@ -308,7 +311,19 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
             const int r = idx;
             if ((lane & (32 / N - 1)) != 0 || r >= rows) continue;
             if (EPI == EPI_PARTIAL) {
-                a.partial[(size_t)r * a.out_stride + unit] = tot;
+                if (a.ar.n > 1) {  // straight into every rank's exchange region (NVLink stores)
+                    const size_t off = kArHeader + ((((size_t)ar_slot * kMaxTp + a.ar.me) * kMaxRows + r) *
+                                                    a.ar.hidden + unit) * 2 * sizeof(uint64_t);
+                    const uint64_t t = (uint64_t)ar_tag << 32;
+                    const uint64_t w0 = t | (uint32_t)(uint64_t)tot, w1 = t | (uint32_t)((uint64_t)tot >> 32);
+                    for (int p = 0; p < a.ar.n; p++) {
+                        uint64_t *d = reinterpret_cast<uint64_t *>(a.ar.base[p] + off);
+                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(w0) : "memory");
+                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d + 1), "l"(w1) : "memory");
+                    }
+                } else {
+                    a.partial[(size_t)r * a.out_stride + unit] = tot;
+                }
             } else {  // EPI_RESID
                 const size_t o = (size_t)r * a.out_stride + unit;
                 a.out[o] = (int16_t)sat16((int32_t)a.resid[o] + round_mac(tot));

@@ -72,6 +72,56 @@ __global__ void k_round_resid(const ResidArgs a) {
         a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(a.partial[i]));
 }
 
+// Peer all-reduce, receiving side (one CTA): every thread polls the tagged
+// words of its elements from every rank (bounded), adds the ranks' exact sums
+// (order-free), rounds as round_mac and adds the residual -- the same result on
+// every rank.  The CTA then counts the all-reduce as done.
+__global__ void __launch_bounds__(1024) k_ar_finish(const ArFinishArgs a) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int fail_s;
+    if (threadIdx.x == 0) fail_s = 0;
+    __syncthreads();
+    const int epoch = *a.ar.epoch, slot = epoch & 1;
+    const uint32_t tag = (uint32_t)epoch + 1u;
+    const int rows = a.step->rows, H = a.ar.hidden;
+    const uint64_t *words = reinterpret_cast<const uint64_t *>(a.ar.base[a.ar.me] + kArHeader) +
+                            (size_t)slot * kMaxTp * kMaxRows * H * 2;
+    for (int i = threadIdx.x; i < rows * H; i += blockDim.x) {
+        int64_t sum = 0;
+        bool ok = true;
+        for (int p = 0; p < a.ar.n && ok; p++) {
+            const uint64_t *w = words + ((size_t)p * kMaxRows * H + i) * 2;
+            uint64_t w0 = 0, w1 = 0;
+            for (uint32_t it = 0;; it++) {
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w0) : "l"(w) : "memory");
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w1) : "l"(w + 1) : "memory");
+                if ((uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag) break;
+                if (it >= (1u << 22) || *(volatile int *)&fail_s) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+            sum += (int64_t)(((w1 & 0xffffffffull) << 32) | (w0 & 0xffffffffull));
+        }
+        if (!ok) {
+            fail_s = 1;
+            atomicCAS(a.error, 0, 5);
+            continue;
+        }
+        a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(sum));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *a.ar.epoch = epoch + 1;
+}
+
+cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s) {
+    ArFinishArgs c = a;
+    void *args[] = {&c};
+    return launch_pdl((const void *)k_ar_finish, dim3(1), dim3(1024), args, s);
+}
+
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {
     ResidArgs c = a;
     void *args[] = {&c};

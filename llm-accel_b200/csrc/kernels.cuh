@@ -24,6 +24,22 @@ enum Epi : int {
     EPI_PARTIAL = 3 // exact int64 partial sums (tensor-parallel ranks)
 };
 
+// Peer all-reduce over NVLink (tensor parallel): each rank owns one exchange
+// region and every rank stores its exact int64 partial sums straight into every
+// rank's region.  Each sum travels as two 64-bit words {32 data bits, 32-bit
+// tag = all-reduce number + 1}; a 64-bit store is single-copy atomic, so the
+// receiver polls the words themselves and needs no fence or flag.  Layout:
+//   256 B header | uint64 word[2 slots][kMaxTp sources][kMaxRows][hidden][2]
+constexpr int kMaxTp = 8;
+constexpr int kArHeader = 256;
+struct ArPeers {
+    char *base[kMaxTp];  // exchange region of every rank (this rank's own included)
+    int n;               // ranks (0: the partial sums stay local, NCCL reduces them)
+    int me;
+    int hidden;
+    int *epoch;          // this rank's count of finished all-reduces (slot = epoch & 1)
+};
+
 struct ProjArgs {
     const uint32_t *w;   // unit-ordered, byte-split weights (see launch_pack_pairs)
     int K;               // input features
@@ -50,6 +66,7 @@ struct ProjArgs {
     int units_per_chunk; // units B per stage / bulk copy
     int parts;           // warps sharing one unit along K (1 or 4); G*B*parts consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
+    ArPeers ar;          // EPI_PARTIAL with ar.n > 1: push the sums to every rank
 };
 
 constexpr int kCluster = 8;         // CTAs per (row, query head) attention cluster
@@ -88,6 +105,15 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
     int n;
     const Step *step;
 };
+
+struct ArFinishArgs {  // wait for every rank's sums, add them, round, + residual
+    ArPeers ar;
+    const int16_t *resid;
+    int16_t *out;
+    const Step *step;
+    int *error;
+};
+cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 
 // Launchers (stream-ordered, programmatic-dependent launch enabled).
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);

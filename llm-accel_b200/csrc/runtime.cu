@@ -85,6 +85,10 @@ struct llmx_ctx {
     int16_t *sc = nullptr;
     int32_t *tmax = nullptr;
     unsigned *bar = nullptr;
+    // peer all-reduce (tensor parallel): exchange regions of every rank (IPC-mapped)
+    ArPeers ar{};
+    char *ar_region = nullptr;
+    std::vector<char *> ar_opened;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -144,6 +148,12 @@ int env_int(const char *name, int def, int lo, int hi) {
 }
 
 int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
+    if (c->ar.n > 1) {  // the projection pushed its sums to every rank: wait, add, round
+        ArFinishArgs f{c->ar, resid, out, c->step, c->err};
+        CK(launch_ar_finish(f, c->stream));
+        c->launches += 1;
+        return LLMX_OK;
+    }
     CKN(ncclAllReduce(c->partial, c->partial, (size_t)rows * c->s.hidden, ncclInt64, ncclSum, c->comm,
                       c->stream));
     ResidArgs r{c->partial, resid, out, c->s.hidden, c->step};
@@ -205,6 +215,7 @@ ProjArgs o_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in) {
     o.out_stride = c->s.hidden;
     o.resid = in;
     o.partial = c->partial;
+    o.ar = c->ar;
     return o;
 }
 
@@ -236,6 +247,7 @@ ProjArgs down_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in)
     d.out_stride = c->s.hidden;
     d.resid = in;
     d.partial = c->partial;
+    d.ar = c->ar;
     return d;
 }
 
@@ -357,12 +369,59 @@ int launch_fused(llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count, int fi
     return LLMX_OK;
 }
 
+// Peer all-reduce set-up: one zeroed exchange region per rank, its IPC handle
+// all-gathered over NCCL, the other ranks' regions mapped.  If a peer region
+// cannot be mapped the context keeps the NCCL all-reduce.
+int setup_peer_allreduce(llmx_ctx *c) {
+    const size_t bytes = kArHeader + (size_t)2 * kMaxTp * kMaxRows * c->s.hidden * 2 * sizeof(uint64_t);
+    int rc;
+    int *epoch = nullptr;
+    char *hbuf = nullptr;
+    if ((rc = dalloc(c, &c->ar_region, bytes)) || (rc = dalloc(c, &epoch, 1)) ||
+        (rc = dalloc(c, &hbuf, (size_t)c->size * sizeof(cudaIpcMemHandle_t))))
+        return rc;
+    CK(cudaMemset(c->ar_region, 0, bytes));
+    CK(cudaMemset(epoch, 0, sizeof(int)));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->ar_region));
+    CK(cudaMemcpy(hbuf + (size_t)c->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    CKN(ncclAllGather(hbuf + (size_t)c->rank * sizeof(mine), hbuf, sizeof(mine), ncclChar, c->comm, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    std::vector<cudaIpcMemHandle_t> all(c->size);
+    CK(cudaMemcpy(all.data(), hbuf, all.size() * sizeof(mine), cudaMemcpyDeviceToHost));
+    ArPeers a{};
+    for (int p = 0; p < c->size; p++) {
+        if (p == c->rank) {
+            a.base[p] = c->ar_region;
+            continue;
+        }
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            for (char *q : c->ar_opened) cudaIpcCloseMemHandle(q);
+            c->ar_opened.clear();
+            return LLMX_OK;  // keep the NCCL all-reduce
+        }
+        a.base[p] = static_cast<char *>(ptr);
+        c->ar_opened.push_back(a.base[p]);
+    }
+    a.n = c->size;
+    a.me = c->rank;
+    a.hidden = c->s.hidden;
+    a.epoch = epoch;
+    c->ar = a;
+    return LLMX_OK;
+}
+
 void release(llmx_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->dev);
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.first);
     c->graphs.clear();
+    for (char *p : c->ar_opened) cudaIpcCloseMemHandle(p);
+    c->ar_opened.clear();
     if (c->comm) ncclCommDestroy(c->comm);
     for (void *p : c->allocations) cudaFree(p);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -552,6 +611,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
             g_last_error = std::string("ncclCommInitRank: ") + ncclGetErrorString(r);
             return bail(LLMX_ERR_NCCL);
         }
+        if (tp_size <= kMaxTp && env_int("LLMX_TP_NCCL", 0, 0, 1) == 0 && (rc = setup_peer_allreduce(c)))
+            return bail(rc);
     }
     *out = c;
     return LLMX_OK;
@@ -765,6 +826,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         case LLMX_KERNEL_ATTN: return launch_attn(attn_args(c, layer), (int)rows, c->stream);
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
+            o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
             set_stages(c, o, ge, rt);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
         }
@@ -775,6 +837,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         }
         case LLMX_KERNEL_DOWN: {
             ProjArgs d = down_args(c, layer, out, in);
+            d.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
             set_stages(c, d, ge, rt);
             return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
         }

@@ -1,7 +1,10 @@
-"""Tensor-parallel stack on two GPUs (NCCL int64 all-reduce after O and Down).
+"""Tensor-parallel stack on two GPUs (int64 all-reduce after O and Down).
 
-Each rank holds its shard of the heads / FFN columns (llmx_create with
-tp_size 2) and runs the same llmx_stack calls; after every call both ranks must
+Two reductions are checked: the default peer all-reduce (O / Down epilogues
+store their exact sums into every rank's IPC-mapped exchange region over
+NVLink, a one-block kernel adds them) and NCCL (LLMX_TP_NCCL=1).  Each rank
+holds its shard of the heads / FFN columns (llmx_create with tp_size 2) and
+runs the same llmx_stack calls; after every call both ranks must
 hold the one-GPU oracle's rows bit for bit (the reduction of exact int64
 partial sums is order-free, rounding happens after it).  Oracle references are
 computed before any collective, so no rank can stop between collectives.
@@ -24,7 +27,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result_dir):
+def _worker(rank, world, port, result_dir, nccl):
     sys.path.insert(0, os.path.join(os.path.dirname(HERE), "llm-accel_b200"))
     sys.path.insert(0, os.path.join(os.path.dirname(HERE), "oracle"))
     sys.path.insert(0, HERE)
@@ -37,6 +40,7 @@ def _worker(rank, world, port, result_dir):
     import oracle as O
     from helpers import OracleState, oracle_shape
 
+    os.environ["LLMX_TP_NCCL"] = str(nccl)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120))
@@ -64,12 +68,13 @@ def _worker(rank, world, port, result_dir):
         f.write("ok" if not bad else f"mismatch at steps {bad}")
 
 
-def test_tensor_parallel_two_gpus_match_oracle(tmp_path):
+@pytest.mark.parametrize("nccl", [0, 1], ids=["peer_allreduce", "nccl_allreduce"])
+def test_tensor_parallel_two_gpus_match_oracle(tmp_path, nccl):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), nccl), nprocs=2, join=True)
     for r in range(2):
         assert (tmp_path / f"rank{r}.txt").read_text() == "ok", f"rank {r}"
