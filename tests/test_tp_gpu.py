@@ -1,14 +1,14 @@
-"""Tensor-parallel stack on two GPUs (int64 all-reduce after O and Down).
+"""Tensor-parallel stack on two and four GPUs (int64 all-reduce after O and Down).
 
 Two reductions are checked: the default peer all-reduce (O / Down epilogues
 store their exact sums into every rank's IPC-mapped exchange region over
 NVLink, a one-block kernel adds them) and NCCL (LLMX_TP_NCCL=1).  Each rank
-holds its shard of the heads / FFN columns (llmx_create with tp_size 2) and
+holds its shard of the heads / FFN columns (llmx_create with tp_size 2 or 4) and
 runs the same llmx_stack calls; after every call both ranks must
 hold the one-GPU oracle's rows bit for bit (the reduction of exact int64
 partial sums is order-free, rounding happens after it).  Oracle references are
 computed before any collective, so no rank can stop between collectives.
-Skipped when fewer than two GPUs are visible.
+Each case is skipped when fewer GPUs than its ranks are visible.
 """
 import os
 import socket
@@ -68,13 +68,14 @@ def _worker(rank, world, port, result_dir, nccl):
         f.write("ok" if not bad else f"mismatch at steps {bad}")
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("nccl", [0, 1], ids=["peer_allreduce", "nccl_allreduce"])
-def test_tensor_parallel_two_gpus_match_oracle(tmp_path, nccl):
+def test_tensor_parallel_gpus_match_oracle(tmp_path, nccl, world):
     torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), nccl), nprocs=2, join=True)
-    for r in range(2):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), nccl), nprocs=world, join=True)
+    for r in range(world):
         assert (tmp_path / f"rank{r}.txt").read_text() == "ok", f"rank {r}"
