@@ -297,7 +297,7 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
     if cpu is not None:
         result["cpu_baseline"] = cpu
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(json.dumps(result))
     acc.close()
     if dist:
         dist.barrier()
@@ -370,7 +370,7 @@ def run_reference(args, cfg_id, world, K, W):
         ref.stack(rows[i:i + 1], P + i)
     dt = time.time() - t0
     v = K / dt
-    print(json.dumps({
+    emit(json.dumps({
         "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": dt * 1e3 / K, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int16", "data": "synthetic (same seeds as the llmx arm)",
@@ -379,10 +379,24 @@ def run_reference(args, cfg_id, world, K, W):
                          "sample": f"{K} decode forwards (36 layers + final norm) at positions {P}..{P + K - 1}, "
                                    f"oracle restatement of the reference golden model, {cores} threads"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    }))
+
+
+_RESULT_FD = None
+
+
+def emit(line):
+    """The one result line, on the process's original standard output."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (line + "\n").encode())
 
 
 def main():
+    global _RESULT_FD
+    # Libraries loaded here (NCCL, CUDA) may print to standard output; send file
+    # descriptor 1 to standard error so that the JSON result is the only line there.
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
