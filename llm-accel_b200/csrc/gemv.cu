@@ -344,7 +344,7 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_
 // consecutive units making a ~32 KiB chunk, and G stages form the ring; the
 // consumer warps are G groups of B.  A unit of 16 KiB or more (the FFN-wide
 // Down rows) fills a stage alone and would leave one warp per stage to digest
-// it, so such units are split over P = 4 warps.  Limits: G*B*P <= consumer
+// it, so such units are split over P = 4 (or, for a deeper ring, 2) warps.  Limits: G*B*P <= consumer
 // warps of the kernel, G >= 2 (double buffering), shared memory within max_smem.
 int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
@@ -353,7 +353,15 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
     int B = (32 * 1024) / unit;
     if (B < 1) B = 1;
     if (B > cmax / 2) B = cmax / 2;
-    const int P = (U == 1 && B == 1 && unit >= 16 * 1024) ? 4 : 1;
+    int P = 1;
+    if (U == 1 && B == 1 && unit >= 16 * 1024) {
+        // stages first (what the ring and shared memory allow), then as many
+        // warps per unit as the stages leave
+        int g0 = ring_bytes / unit;
+        if (g0 < 2) g0 = 2;
+        while (g0 > 2 && gemv_smem_bytes(rows_tmpl, epi, K, g0, 1, 4) > (size_t)max_smem) g0--;
+        P = cmax / g0 >= 4 ? 4 : (cmax / g0 >= 2 ? 2 : 1);
+    }
     int G = ring_bytes / (B * unit);
     if (G > cmax / (B * P)) G = cmax / (B * P);
     if (G < 2) G = 2;
@@ -393,6 +401,11 @@ static cudaError_t launch_gemv_t(const ProjArgs &a, int grid, cudaStream_t st) {
                 if (a.K == 11008) return launch_gemv_v<R, EPI, 43, 4>(a, grid, st);
             return launch_gemv_v<R, EPI, 0, 4>(a, grid, st);
         }
+        if (a.parts == 2) {
+            if constexpr (R <= 2)
+                if (a.K == 11008) return launch_gemv_v<R, EPI, 43, 2>(a, grid, st);
+            return launch_gemv_v<R, EPI, 0, 2>(a, grid, st);
+        }
         if constexpr (R <= 2)
             if (a.K == 11008 && a.parts == 1) return launch_gemv_v<R, EPI, 43, 1>(a, grid, st);
     }
@@ -429,8 +442,10 @@ static cudaError_t configure_r(int bytes) {
         if (R <= 2) {
             if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 1>, kAttr, bytes))) return e;
             if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 4>, kAttr, bytes))) return e;
+            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 2>, kAttr, bytes))) return e;
         }
         if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 0, 4>, kAttr, bytes))) return e;
+        if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 0, 2>, kAttr, bytes))) return e;
     }
     return cudaFuncSetAttribute(k_gemv<R, EPI, 0, 1>, kAttr, bytes);
 }

@@ -64,7 +64,7 @@ struct ProjArgs {
     int max_seq;
     int stages;          // shared-memory ring stages G (gemv_stages)
     int units_per_chunk; // units B per stage / bulk copy
-    int parts;           // warps sharing one unit along K (1 or 4); G*B*parts consumer warps
+    int parts;           // warps sharing one unit along K (1, 2 or 4); G*B*parts consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
     ArPeers ar;          // EPI_PARTIAL with ar.n > 1: push the sums to every rank
 };
