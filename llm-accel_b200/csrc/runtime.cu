@@ -77,7 +77,7 @@ struct llmx_ctx {
     int64_t *partial = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
-    int ring_kb = 96, ring_wide_kb = 176, gemv_ctas_per_sm = 1;
+    int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
     // fused one-row decode (stack.cu): plan, scratch, barrier counter
     bool fused = false;
     StackArgs stack{};
@@ -128,7 +128,7 @@ constexpr int kProjSmem = 225 * 1024;  // 227 KiB per CTA minus the kernels' sta
 
 // Persistent projection CTAs: gemv_ctas_per_sm per SM (LLMX_GEMV_CTAS_PER_SM),
 // each streaming through a ring of about ring_kb KiB (LLMX_RING_KB; LLMX_RING_WIDE_KB
-// for the FFN-wide Down projection).
+// for the FFN-wide Down projection, LLMX_RING_GU_KB for Gate/Up).
 int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
     (void)rt;
     (void)K;
@@ -138,7 +138,7 @@ int grid_for(llmx_ctx *c, int npairs, int rt, int K) {
 void set_stages(llmx_ctx *c, ProjArgs &a, int epi, int rt) {
     const int smem = kProjSmem / c->gemv_ctas_per_sm - 1024;
     // FFN-wide inputs (the Down projection) may take their own ring size
-    const int ring = a.K > 4 * c->s.hidden ? c->ring_wide_kb : c->ring_kb;
+    const int ring = a.K > 4 * c->s.hidden ? c->ring_wide_kb : (epi == EPI_SILU ? c->ring_gu_kb : c->ring_kb);
     a.stages = gemv_stages(rt, epi, a.K, smem, ring * 1024, &a.units_per_chunk, &a.parts);
     a.error = c->err;
 }
@@ -474,6 +474,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->layer_loaded.assign(s.layers, false);
     c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
     c->ring_wide_kb = env_int("LLMX_RING_WIDE_KB", 176, 8, 200);  // measured best for Down on B200
+    c->ring_gu_kb = env_int("LLMX_RING_GU_KB", c->ring_kb, 8, 200);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     auto bail = [&](int code) {
         release(c);
