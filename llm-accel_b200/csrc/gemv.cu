@@ -30,11 +30,11 @@
 
 namespace llmx {
 
-// Consumer warps per CTA: 16 for decode-sized row counts (latency hiding),
-// 8 for blocks of >= 4 rows (register budget of the 8-row accumulators).
+// Consumer warps per CTA: up to 16 (latency hiding; the 8-row accumulators fit
+// the register budget of 17 warps).
 template <int R>
 struct Warps {
-    static constexpr int kConsumers = R <= 2 ? 16 : 8;
+    static constexpr int kConsumers = 16;
     static constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
 };
 // Activation prologue (consumer warps): rows -> shared memory, RMS-normalised
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     pdl_wait();
     pdl_trigger();
     const Step st = *a.step;
-    const int rows = st.rows;
+    const int rows = st.rows - a.row0;  // rows of this launch (a block may be split in row groups)
     const int ar_epoch = (EPI == EPI_PARTIAL && a.ar.n > 1) ? *a.ar.epoch : 0;
     const int ar_slot = ar_epoch & 1;
     const uint32_t ar_tag = (uint32_t)ar_epoch + 1u;
@@ -349,7 +349,7 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_
 int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const int unit = U * K * 2;
-    const int cmax = rows_tmpl <= 2 ? 16 : 8;
+    const int cmax = 16;
     int B = (32 * 1024) / unit;
     if (B < 1) B = 1;
     if (B > cmax / 2) B = cmax / 2;

@@ -67,6 +67,7 @@ struct ProjArgs {
     int parts;           // warps sharing one unit along K (1, 2 or 4); G*B*parts consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
     ArPeers ar;          // EPI_PARTIAL with ar.n > 1: push the sums to every rank
+    int row0;            // first row of this launch (x / out / resid already offset)
 };
 
 constexpr int kCluster = 8;         // CTAs per (row, query head) attention cluster

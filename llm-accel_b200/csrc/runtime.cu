@@ -279,9 +279,24 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         set_stages(c, g, EPI_SILU, rt);
         CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
         ProjArgs d = down_args(c, layer, out, in);
-        set_stages(c, d, ge, rt);
-        CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
-        c->launches += 2;
+        if (rt == 8 && c->size == 1) {
+            // an 8-row block as two 4-row launches: 8 FFN-wide activation rows would
+            // fill shared memory and starve the weight ring; 4 rows leave it room
+            for (int half = 0; half < 2; half++) {
+                ProjArgs h = d;
+                h.row0 = 4 * half;
+                h.x += (size_t)h.row0 * c->Il;
+                h.out += (size_t)h.row0 * c->s.hidden;
+                h.resid += (size_t)h.row0 * c->s.hidden;
+                set_stages(c, h, ge, 4);
+                CK(launch_proj(h, ge, 4, grid_for(c, h.npairs, 4, h.K), c->stream));
+            }
+            c->launches += 3;
+        } else {
+            set_stages(c, d, ge, rt);
+            CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
+            c->launches += 2;
+        }
         if (c->size > 1) return allreduce_resid(c, rows, out, in);
         return LLMX_OK;
     }
