@@ -138,22 +138,36 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     __syncthreads();
 
     // ---- 1. scores; owned tile maxima pushed to every CTA of the cluster ----
+    // Banks k mod 4 of golden_attention_mm saturate in k order; a bank holds <= 32
+    // products of magnitude <= 2^26 at head_dim <= 128, so no partial sum of <= 31
+    // of them leaves int32 and the in-order saturating bank equals sat32 of its
+    // exact sum.  Each bank is therefore summed as two exact int32 halves (even /
+    // odd 16-byte vectors, <= 16 products each), added in int64 and saturated once.
     for (int pp = threadIdx.x; pp < npos; pp += blockDim.x) {
         const uint4 *qv = reinterpret_cast<const uint4 *>(m.q);
         const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
-        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;  // banks k mod 4, saturating, in k order
-        for (int e8 = 0; e8 < vpr; e8++) {
-            const uint4 q = qv[e8], k = kv[e8];
-            b0 = add_sat(b0, qk_prod(lo16(q.x), q412(lo16(k.x))));
-            b1 = add_sat(b1, qk_prod(hi16(q.x), q412(hi16(k.x))));
-            b2 = add_sat(b2, qk_prod(lo16(q.y), q412(lo16(k.y))));
-            b3 = add_sat(b3, qk_prod(hi16(q.y), q412(hi16(k.y))));
-            b0 = add_sat(b0, qk_prod(lo16(q.z), q412(lo16(k.z))));
-            b1 = add_sat(b1, qk_prod(hi16(q.z), q412(hi16(k.z))));
-            b2 = add_sat(b2, qk_prod(lo16(q.w), q412(lo16(k.w))));
-            b3 = add_sat(b3, qk_prod(hi16(q.w), q412(hi16(k.w))));
+        int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        auto add8 = [&](int32_t (&c)[4], const uint4 q, const uint4 k) {
+            c[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
+            c[1] += qk_prod(hi16(q.x), q412(hi16(k.x)));
+            c[2] += qk_prod(lo16(q.y), q412(lo16(k.y)));
+            c[3] += qk_prod(hi16(q.y), q412(hi16(k.y)));
+            c[0] += qk_prod(lo16(q.z), q412(lo16(k.z)));
+            c[1] += qk_prod(hi16(q.z), q412(hi16(k.z)));
+            c[2] += qk_prod(lo16(q.w), q412(lo16(k.w)));
+            c[3] += qk_prod(hi16(q.w), q412(hi16(k.w)));
+        };
+        int e8 = 0;
+#pragma unroll 2
+        for (; e8 + 1 < vpr; e8 += 2) {
+            add8(b[0], qv[e8], kv[e8]);
+            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
         }
-        int32_t tot = sat32((int64_t)b0 + b1 + b2 + b3);
+        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        int64_t t64 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
+        int32_t tot = sat32(t64);
         tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));  // x accum(fm(1/sqrt(d)))
         const int32_t sc = sat16(rnd(tot, 8));
         m.sc[pp] = (int16_t)sc;
