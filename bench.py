@@ -254,6 +254,10 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
     step_bytes = [bytes_per_decode(shape, world, P + i + 1) for i in range(K)]
     dec_gbs = sum(step_bytes) / (decode_ms * 1e-3) / 1e9
 
+    gen = None
+    if world == 1:
+        gen = generate_leg(acc, model, shape, prompt, device_time, stream)
+
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(acc, model, shape, rows[P:], P, e2e_outputs)
@@ -294,6 +298,8 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
         "clocks": clock,
         "setup_s": setup_s,
     }
+    if gen is not None:
+        result["generate"] = gen
     if cpu is not None:
         result["cpu_baseline"] = cpu
     if rank == 0:
@@ -302,6 +308,51 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def generate_leg(acc, model, shape, prompt, device_time, stream, new_tokens=64):
+    """Greedy generation on the device (llmx_generate): the prompt in P8 blocks,
+    then new_tokens tokens, each an LM-head argmax over the tied 151,936-row
+    table fed back as a decode row.  Per-token cost = (T(1 + n) - T(1)) / n, so
+    the prompt's cost cancels.  The host argmax of the same row is timed once
+    beside it (the reference's sampler runs on the host)."""
+    import torch
+    import llmx
+
+    t0 = time.time()
+    acc.upload_vocab(model)
+    upload_s = time.time() - t0
+    prompt = [int(t) for t in prompt]
+    acc.generate(prompt, 2)                     # warm-up: graphs, argmax kernels
+    toks = [None, None]
+
+    def run(n, slot):
+        toks[slot] = acc.generate(prompt, n)
+    t1 = device_time(lambda: run(1, 0))
+    tn = device_time(lambda: run(1 + new_tokens, 1))
+    assert toks[1][0] == toks[0][0]
+    # the argmax alone on one final-normed row already on the device
+    h_row = acc.hidden_ptr(0)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    table = llmx.lib().llmx_model_embedding(model.h)
+    w = torch.from_numpy(np.ctypeslib.as_array(table, shape=(shape.vocab, shape.hidden)).copy()).cuda()
+    for _ in range(3):
+        llmx.lm_head_argmax_device(h_row, 1, shape.hidden, w.data_ptr(), shape.vocab, tok.data_ptr(), acc.stream)
+    reps = 20
+    am_ms = device_time(lambda: [llmx.lm_head_argmax_device(h_row, 1, shape.hidden, w.data_ptr(), shape.vocab,
+                                                            tok.data_ptr(), acc.stream) for _ in range(reps)]) / reps
+    row = acc.read_hidden(0, 1)[0]
+    t0 = time.time()
+    host_tok = model.lm_head_argmax(row)
+    host_ms = (time.time() - t0) * 1e3
+    assert host_tok == int(tok.item()), "device argmax differs from the host argmax"
+    del w
+    return {"value": new_tokens / ((tn - t1) * 1e-3), "unit": "tok/s", "new_tokens": new_tokens,
+            "prompt_tokens": len(prompt), "ms_prompt_plus_first_token": t1,
+            "ms_per_token": (tn - t1) / new_tokens,
+            "lm_head_argmax_ms": am_ms, "lm_head_gbs": shape.vocab * shape.hidden * 2 / (am_ms * 1e-3) / 1e9,
+            "host_lm_head_argmax_ms": host_ms, "host_threads": os.cpu_count(), "vocab_upload_s": upload_s,
+            "api": "llmx_generate (device embedding gather + stack + LM-head argmax, one host wait)"}
 
 
 def cpu_baseline(acc, model, shape, dec_rows, P, gpu_outputs):

@@ -267,6 +267,32 @@ int llmx_run_prompt_block(llmx_ctx *ctx, const llmx_model *m, const uint32_t *to
 int llmx_run_token(llmx_ctx *ctx, const llmx_model *m, uint32_t token,
                    uint32_t position, int16_t *hidden_out);
 
+/* ---------------------------------------------------------------------------
+ * Greedy generation on the device: the coarse-task branch of the reference's
+ * generate mode (main, host:9016-9132), with the embedding gather
+ * (model_data_t::embedding host:871-884) and the LM-head argmax
+ * (model_data_t::lm_head_argmax host:937-977) moved onto the GPU.  Same
+ * tokens as the host loop; the host waits once, at the end.
+ * ------------------------------------------------------------------------- */
+/* Copies the model's token-embedding table and LM head (the embedding itself
+ * when tied) into device memory owned by the context: 2 * vocab * hidden bytes,
+ * twice that when untied.  A synthetic model's embedding is materialised on the
+ * host first.  May be called again to replace the tables. */
+int llmx_upload_vocab(llmx_ctx *ctx, llmx_model *m);
+/* Prompt tokens in blocks of block_rows (1..8) rows at positions 0, block_rows,
+ * ... (run_prompt_block host:7840-7918; only the last block is final-normed),
+ * then max_new tokens: each is the argmax of the previous final-normed row and,
+ * except the last, runs as one decode row (run_token host:7665-7700) at the
+ * next position.  layer_count 0 = every layer (the executor's --layers,
+ * host:7621-7640).  out_tokens[max_new]; last_block_out (may be NULL) receives
+ * the last prompt block's final-normed rows [rows][hidden], whose per-row
+ * FNV-1a checksums the reference prints (host:9042-9057).  Needs
+ * n_prompt + max_new - 1 <= max_seq, uploaded layers [0, layer_count), norms
+ * and llmx_upload_vocab.  All ranks of a tensor-parallel group call it with
+ * the same arguments. */
+int llmx_generate(llmx_ctx *ctx, const uint32_t *prompt, uint32_t n_prompt, uint32_t block_rows,
+                  uint32_t layer_count, uint32_t max_new, uint32_t *out_tokens, int16_t *last_block_out);
+
 #ifdef __cplusplus
 }
 #endif

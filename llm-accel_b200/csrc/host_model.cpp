@@ -171,6 +171,22 @@ using namespace llmx;
 // --------------------------------------------------------------------------
 // C ABI: model container
 // --------------------------------------------------------------------------
+const int16_t *llmx::model_embedding_table(llmx_model *m) {
+    const llmx_shape &s = m->shape;
+    if (m->embedding.empty() && m->kind == 2) {
+        // synthetic model: materialise the N(0, 1) Q8.8 rows once
+        m->embedding.resize((size_t)s.vocab * s.hidden);
+        const GaussSampler emb(256.0);
+        emb.fill(m->gseed, kGaussStreamEmbedding, 0, m->embedding.data(), m->embedding.size(), host_threads());
+    }
+    return m->embedding.empty() ? nullptr : m->embedding.data();
+}
+
+const int16_t *llmx::model_lm_head_table(llmx_model *m) {
+    if (!m->tied) return m->lm_head.empty() ? nullptr : m->lm_head.data();
+    return model_embedding_table(m);
+}
+
 extern "C" {
 
 size_t llmx_layer_weight_elems(const llmx_shape *shape) { return shape ? layer_elems(*shape) : 0; }
@@ -340,17 +356,7 @@ int llmx_model_embed(const llmx_model *m, const uint32_t *tokens, uint32_t n, in
 int llmx_model_lm_head_argmax(const llmx_model *m, const int16_t *h, int threads, uint32_t *token) {
     if (!m || !h || !token) return LLMX_ERR_ARG;
     const llmx_shape &s = m->shape;
-    const int16_t *w = nullptr;
-    if (!m->tied) w = m->lm_head.data();
-    else if (!m->embedding.empty()) w = m->embedding.data();
-    else if (m->kind == 2) {
-        // tied synthetic embedding: materialise it once
-        llmx_model *mm = const_cast<llmx_model *>(m);
-        mm->embedding.resize((size_t)s.vocab * s.hidden);
-        const GaussSampler emb(256.0);
-        emb.fill(m->gseed, kGaussStreamEmbedding, 0, mm->embedding.data(), mm->embedding.size(), host_threads());
-        w = m->embedding.data();
-    }
+    const int16_t *w = model_lm_head_table(const_cast<llmx_model *>(m));
     if (!w) return LLMX_ERR_STATE;
     const int T = threads > 0 ? threads : host_threads();
     std::vector<int64_t> best(T, std::numeric_limits<int64_t>::min());

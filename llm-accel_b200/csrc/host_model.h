@@ -37,6 +37,12 @@ struct GaussSampler {
     void fill(uint64_t seed, uint64_t stream, uint64_t index0, int16_t *out, size_t n, int threads) const;
 };
 
+// The model's [vocab][hidden] token-embedding table, materialised first for a
+// synthetic model whose rows are otherwise generated on demand; nullptr when the
+// model has none.  The LM head is that table when tied, else the separate head.
+const int16_t *model_embedding_table(llmx_model *m);
+const int16_t *model_lm_head_table(llmx_model *m);
+
 // Tables shared by every context (host-built, uploaded once).
 void build_exp_tables(int16_t *e16_8, int16_t *p18_4);
 void build_rope_table(int head_dim, int max_seq, int16_t *table);

@@ -130,6 +130,30 @@ cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {
 }
 
 // --------------------------------------------------------------------------
+// token embedding gather (model_data_t::embedding host:871-884): one block per
+// row, 16-byte copies of the table row of that row's token id
+// --------------------------------------------------------------------------
+__global__ void k_embed_rows(const int16_t *__restrict__ table, const uint32_t *__restrict__ tokens, int hidden,
+                             unsigned vocab, int16_t *__restrict__ out, int *err) {
+    const uint32_t t = tokens[blockIdx.x];
+    uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)blockIdx.x * hidden);
+    const int nvec = hidden >> 3;
+    if (t >= vocab) {
+        for (int i = threadIdx.x; i < nvec; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+        if (threadIdx.x == 0) atomicExch(err, kErrTokenRange);
+        return;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(table + (size_t)t * hidden);
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) dst[i] = src[i];
+}
+
+cudaError_t launch_embed_rows(const int16_t *table, const uint32_t *tokens, int rows, int hidden, unsigned vocab,
+                              int16_t *out, int *err, cudaStream_t s) {
+    k_embed_rows<<<rows, 256, 0, s>>>(table, tokens, hidden, vocab, out, err);
+    return cudaGetLastError();
+}
+
+// --------------------------------------------------------------------------
 // weight layout
 // --------------------------------------------------------------------------
 __global__ void k_pack_pairs(const int16_t *__restrict__ dense, int ld, int col0, int K,

@@ -165,6 +165,17 @@ cudaError_t stack_configure(size_t smem);
 cudaError_t launch_stack(const StackArgs &a, size_t smem, int grid, cudaStream_t s);
 int stack_threads();
 
+// Greedy generation on the device (lm_head.cu, kernels.cu).  LM-head argmax
+// over caller-owned scratch of lm_argmax_scratch_bytes(); token-embedding
+// gather of rows tokens[0..rows) (a token id >= vocab sets *err to
+// kErrTokenRange and writes a zero row).
+constexpr int kErrTokenRange = 7;
+size_t lm_argmax_scratch_bytes();
+cudaError_t launch_lm_argmax(const int16_t *h, int rows, int hidden, const int16_t *w, unsigned vocab,
+                             uint32_t *tokens, void *scratch, int nsm, cudaStream_t s);
+cudaError_t launch_embed_rows(const int16_t *table, const uint32_t *tokens, int rows, int hidden, unsigned vocab,
+                              int16_t *out, int *err, cudaStream_t s);
+
 // Message returned by llmx_last_error() on this thread.
 void set_last_error(const std::string &msg);
 

@@ -30,6 +30,7 @@ namespace {
 constexpr int kPickRows = 8;           // rows per call (the controller's block size)
 constexpr int kScanBlocks = 1024;      // upper bound of the scan grid
 constexpr int kScanThreads = 256;
+constexpr int kScanBlocksPerSm = 2;    // resident scan blocks per SM (about 100 registers a thread)
 constexpr int kMaxDevices = 64;
 
 struct Best {
@@ -60,10 +61,15 @@ static __device__ __forceinline__ long long dot8(uint4 h, uint4 w) {
     return s;
 }
 
+// Each warp scores V consecutive vocabulary rows per iteration, with every
+// 16-byte load of those rows (8 per lane per 4 KiB row) issued before the dot
+// products, so that enough of the table is in flight to stream it at HBM rate.
 template <int R>
-__global__ void __launch_bounds__(kScanThreads) k_lm_scan(const int16_t *__restrict__ h, int hidden,
-                                                          const int16_t *__restrict__ w, unsigned vocab,
-                                                          int rows, Best *__restrict__ part) {
+__global__ void __launch_bounds__(kScanThreads, kScanBlocksPerSm)
+    k_lm_scan(const int16_t *__restrict__ h, int hidden, const int16_t *__restrict__ w, unsigned vocab, int rows,
+              Best *__restrict__ part) {
+    constexpr int V = R <= 2 ? 2 : 1;  // vocabulary rows per warp iteration
+    constexpr int J = 8;               // 16-byte loads per lane per row and chunk
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const unsigned v0 = (unsigned)((unsigned long long)vocab * blockIdx.x / gridDim.x);
     const unsigned v1 = (unsigned)((unsigned long long)vocab * (blockIdx.x + 1) / gridDim.x);
@@ -76,25 +82,48 @@ __global__ void __launch_bounds__(kScanThreads) k_lm_scan(const int16_t *__restr
         best[r] = LLONG_MIN;
         arg[r] = 0xffffffffu;
     }
-    for (unsigned v = v0 + warp; v < v1; v += nw) {
-        const uint4 *wr = reinterpret_cast<const uint4 *>(w + (size_t)v * hidden);
-        long long acc[R];
+    for (unsigned v = v0 + (unsigned)warp * V; v < v1; v += (unsigned)nw * V) {
+        long long acc[V][R];
 #pragma unroll
-        for (int r = 0; r < R; r++) acc[r] = 0;
-#pragma unroll 8
-        for (int k = lane; k < nvec; k += 32) {
-            const uint4 wv = llmx::ld_stream(wr + k);
+        for (int u = 0; u < V; u++)
 #pragma unroll
-            for (int r = 0; r < R; r++)
-                if (r < rows) acc[r] += dot8(__ldg(h4 + (size_t)r * nvec + k), wv);
+            for (int r = 0; r < R; r++) acc[u][r] = 0;
+        for (int kb = 0; kb < nvec; kb += 32 * J) {
+            uint4 wv[V][J];
+#pragma unroll
+            for (int u = 0; u < V; u++) {
+                const uint4 *wr = reinterpret_cast<const uint4 *>(w + (size_t)(v + u) * hidden);
+#pragma unroll
+                for (int j = 0; j < J; j++) {
+                    const int k = kb + j * 32 + lane;
+                    wv[u][j] = (k < nvec && v + u < v1) ? llmx::ld_stream(wr + k) : make_uint4(0, 0, 0, 0);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < J; j++) {
+                const int k = kb + j * 32 + lane;
+                if (k < nvec) {
+#pragma unroll
+                    for (int r = 0; r < R; r++)
+                        if (r < rows) {
+                            const uint4 hv = __ldg(h4 + (size_t)r * nvec + k);
+#pragma unroll
+                            for (int u = 0; u < V; u++) acc[u][r] += dot8(hv, wv[u][j]);
+                        }
+                }
+            }
         }
 #pragma unroll
-        for (int r = 0; r < R; r++) {
+        for (int u = 0; u < V; u++) {
 #pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) acc[r] += llmx::shfl_xor64(acc[r], o);
-            if (acc[r] > best[r]) {  // this warp visits its tokens in increasing order
-                best[r] = acc[r];
-                arg[r] = v;
+            for (int r = 0; r < R; r++) {
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) acc[u][r] += llmx::shfl_xor64(acc[u][r], o);
+                // this warp visits its tokens in increasing order: '>' keeps the first maximum
+                if (v + u < v1 && acc[u][r] > best[r]) {
+                    best[r] = acc[u][r];
+                    arg[r] = v + u;
+                }
             }
         }
     }
@@ -170,6 +199,29 @@ cudaError_t launch_scan(const int16_t *h, int hidden, const int16_t *w, unsigned
 
 }  // namespace
 
+// The same two kernels on scratch owned by the caller (a context's generate
+// loop), so that contexts on different streams never share partial results.
+size_t llmx::lm_argmax_scratch_bytes() { return sizeof(Best) * kPickRows * kScanBlocks; }
+
+cudaError_t llmx::launch_lm_argmax(const int16_t *h, int rows, int hidden, const int16_t *w, unsigned vocab,
+                                   uint32_t *tokens, void *scratch, int nsm, cudaStream_t s) {
+    if (rows < 1 || rows > kPickRows) return cudaErrorInvalidValue;
+    long long grid = (long long)nsm * kScanBlocksPerSm;
+    if (grid > kScanBlocks) grid = kScanBlocks;
+    if (grid > (long long)vocab) grid = vocab;
+    Best *part = static_cast<Best *>(scratch);
+    cudaError_t e;
+    switch (rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8) {
+    case 1: e = launch_scan<1>(h, hidden, w, vocab, rows, part, (int)grid, s); break;
+    case 2: e = launch_scan<2>(h, hidden, w, vocab, rows, part, (int)grid, s); break;
+    case 4: e = launch_scan<4>(h, hidden, w, vocab, rows, part, (int)grid, s); break;
+    default: e = launch_scan<8>(h, hidden, w, vocab, rows, part, (int)grid, s); break;
+    }
+    if (e != cudaSuccess) return e;
+    k_lm_pick<<<1, kPickRows * 32, 0, s>>>(part, (int)grid, rows, tokens);
+    return cudaGetLastError();
+}
+
 extern "C" int llmx_lm_head_argmax_device(const int16_t *hidden, uint32_t rows, uint32_t hidden_size,
                                           const int16_t *lm_head, uint32_t vocab, uint32_t *tokens,
                                           void *stream) {
@@ -206,9 +258,9 @@ extern "C" int llmx_lm_head_argmax_device(const int16_t *hidden, uint32_t rows, 
         su = g_setup[dev];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // 4 blocks of 8 warps per SM keep enough 16-byte loads in flight to stream the
-    // table at HBM rate; never more blocks than the scratch holds or than rows.
-    long long grid = (long long)su.nsm * 4;
+    // one wave of resident blocks (each warp keeps two 4 KiB rows in flight);
+    // never more blocks than the scratch holds or than vocabulary rows
+    long long grid = (long long)su.nsm * kScanBlocksPerSm;
     if (grid > kScanBlocks) grid = kScanBlocks;
     if (grid > (long long)vocab) grid = vocab;
     const int R = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;

@@ -96,6 +96,11 @@ struct llmx_ctx {
     uint64_t launches = 0, last_launches = 0, device_bytes = 0;
     std::map<std::tuple<uint32_t, uint32_t, uint32_t, int>, std::pair<cudaGraphExec_t, uint64_t>> graphs;
     std::vector<void *> allocations;
+    // device generate loop: vocabulary tables, argmax scratch, token ids by position
+    int16_t *emb_dev = nullptr, *head_dev = nullptr, *gen_rows = nullptr;
+    void *lm_scratch = nullptr;
+    uint32_t *tok_dev = nullptr;
+    bool vocab_loaded = false;
 };
 
 namespace {
@@ -323,6 +328,10 @@ int check_device_error(llmx_ctx *c) {
     CK(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (v != 0) {
         CK(cudaMemset(c->err, 0, sizeof(int)));
+        if (v == kErrTokenRange) {
+            g_last_error = "a token id reached the embedding gather outside the vocabulary";
+            return LLMX_ERR_RANGE;
+        }
         g_last_error = "a kernel's bounded wait expired (code " + std::to_string(v) + ")";
         return LLMX_ERR_TIMEOUT;
     }
@@ -385,6 +394,16 @@ int launch_fused(llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count, int fi
     CK(launch_stack(a, c->stack_smem, c->nsm, c->stream));
     c->launches += 1;
     return LLMX_OK;
+}
+
+// Step record + the stack (fused kernel for one row when enabled, else the
+// captured graph).  Arguments already validated.
+int launch_stack_at(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, uint32_t position,
+                    int final_norm) {
+    int rc = set_step(c, position, rows);
+    if (rc) return rc;
+    if (use_fused(c, rows)) return launch_fused(c, layer_begin, layer_count, final_norm);
+    return launch_stack_graph(c, rows, layer_begin, layer_count, final_norm);
 }
 
 // Peer all-reduce set-up: one zeroed exchange region per rank, its IPC handle
@@ -779,11 +798,7 @@ int llmx_stack_async(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t 
     if (!model_ready(c, layer_begin, layer_count)) return LLMX_ERR_STATE;
     CK(cudaSetDevice(c->dev));
     const uint64_t before = c->launches;
-    int rc = set_step(c, position, rows);
-    if (!rc && use_fused(c, rows))
-        rc = launch_fused(c, layer_begin, layer_count, include_final_norm ? 1 : 0);
-    else if (!rc)
-        rc = launch_stack_graph(c, rows, layer_begin, layer_count, include_final_norm ? 1 : 0);
+    const int rc = launch_stack_at(c, rows, layer_begin, layer_count, position, include_final_norm ? 1 : 0);
     c->last_launches = c->launches - before;
     return rc;
 }
@@ -904,6 +919,99 @@ int llmx_run_token(llmx_ctx *c, const llmx_model *m, uint32_t token, uint32_t po
     int rc = llmx_model_embed(m, &token, 1, row.data());
     if (rc) return rc;
     return llmx_stack(c, row.data(), 1, 0, (uint32_t)c->s.layers, position, 1, 1, hidden_out, nullptr);
+}
+
+int llmx_upload_vocab(llmx_ctx *c, llmx_model *m) {
+    if (!c || !m) return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s, &ms = m->shape;
+    if (ms.hidden != s.hidden || ms.vocab != s.vocab) {
+        g_last_error = "upload_vocab: model hidden size / vocabulary differ from the context's shape";
+        return LLMX_ERR_ARG;
+    }
+    const int16_t *emb = model_embedding_table(m);
+    const int16_t *head = model_lm_head_table(m);
+    if (!emb || !head) {
+        g_last_error = "upload_vocab: the model holds no embedding table or LM head";
+        return LLMX_ERR_STATE;
+    }
+    CK(cudaSetDevice(c->dev));
+    const size_t n = (size_t)s.vocab * s.hidden;
+    int rc = LLMX_OK;
+    if (!c->emb_dev) {
+        if ((rc = dalloc(c, &c->emb_dev, n)) || (rc = dalloc(c, &c->gen_rows, (size_t)LLMX_MAX_ROWS * s.hidden)) ||
+            (rc = dalloc(c, &c->tok_dev, (size_t)s.max_seq + LLMX_MAX_ROWS)))
+            return rc;
+        char *scratch = nullptr;
+        if ((rc = dalloc(c, &scratch, lm_argmax_scratch_bytes()))) return rc;
+        c->lm_scratch = scratch;
+    }
+    if (head != emb && (!c->head_dev || c->head_dev == c->emb_dev)) {
+        if ((rc = dalloc(c, &c->head_dev, n))) return rc;
+    }
+    CK(cudaMemcpy(c->emb_dev, emb, n * 2, cudaMemcpyHostToDevice));
+    if (head == emb) {
+        c->head_dev = c->emb_dev;
+    } else {
+        CK(cudaMemcpy(c->head_dev, head, n * 2, cudaMemcpyHostToDevice));
+    }
+    c->vocab_loaded = true;
+    return LLMX_OK;
+}
+
+int llmx_generate(llmx_ctx *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t block_rows, uint32_t layer_count,
+                  uint32_t max_new, uint32_t *out_tokens, int16_t *last_block_out) {
+    if (!c || !prompt || n_prompt == 0 || block_rows == 0 || block_rows > LLMX_MAX_ROWS ||
+        (max_new && !out_tokens))
+        return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s;
+    const uint32_t L = layer_count ? layer_count : (uint32_t)s.layers;
+    if (L > (uint32_t)s.layers) return LLMX_ERR_ARG;  // "--layers exceeds the selected profile" host:7638-7640
+    // decode forwards run at positions n_prompt .. n_prompt + max_new - 2
+    if ((uint64_t)n_prompt + (max_new ? max_new - 1 : 0) > (uint64_t)s.max_seq) return LLMX_ERR_ARG;
+    for (uint32_t i = 0; i < n_prompt; i++)
+        if (prompt[i] >= (uint32_t)s.vocab) return LLMX_ERR_ARG;
+    if (!c->vocab_loaded || !model_ready(c, 0, L)) return LLMX_ERR_STATE;
+    CK(cudaSetDevice(c->dev));
+    const uint64_t before = c->launches;
+    const int H = s.hidden;
+    CK(cudaMemcpyAsync(c->tok_dev, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream));
+    int rc = LLMX_OK;
+    // prompt in blocks of block_rows rows; only the last block is final-normed (host:9018-9063)
+    uint32_t last_rows = 0;
+    for (uint32_t b0 = 0; b0 < n_prompt && !rc; b0 += block_rows) {
+        const uint32_t n = std::min(block_rows, n_prompt - b0);
+        const int last = b0 + n == n_prompt;
+        CK(launch_embed_rows(c->emb_dev, c->tok_dev + b0, (int)n, H, (unsigned)s.vocab, c->hid[1], c->err,
+                             c->stream));
+        c->launches += 1;
+        rc = launch_stack_at(c, n, 0, L, b0, last);
+        last_rows = n;
+    }
+    if (!rc && last_block_out)
+        CK(cudaMemcpyAsync(c->gen_rows, c->hid[0], (size_t)last_rows * H * 2, cudaMemcpyDeviceToDevice, c->stream));
+    // greedy decode (host:9087-9132): argmax of the last final-normed row, fed back
+    // as one decode row unless it is the last token asked for
+    const int16_t *h = c->hid[0] + (size_t)(last_rows - 1) * H;
+    for (uint32_t step = 0; step < max_new && !rc; step++) {
+        uint32_t *tok = c->tok_dev + n_prompt + step;
+        CK(launch_lm_argmax(h, 1, H, c->head_dev, (unsigned)s.vocab, tok, c->lm_scratch, c->nsm, c->stream));
+        c->launches += 2;
+        if (step + 1 == max_new) break;
+        CK(launch_embed_rows(c->emb_dev, tok, 1, H, (unsigned)s.vocab, c->hid[1], c->err, c->stream));
+        c->launches += 1;
+        rc = launch_stack_at(c, 1, 0, L, n_prompt + step, 1);
+        h = c->hid[0];
+    }
+    c->last_launches = c->launches - before;
+    if (rc) return rc;
+    if (max_new)
+        CK(cudaMemcpyAsync(out_tokens, c->tok_dev + n_prompt, (size_t)max_new * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+    if (last_block_out)
+        CK(cudaMemcpyAsync(last_block_out, c->gen_rows, (size_t)last_rows * H * 2, cudaMemcpyDeviceToHost,
+                           c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
 }
 
 }  // extern "C"

@@ -122,6 +122,8 @@ def lib():
             "llmx_run_prompt_block": (C.c_int, [vp, vp, u32p, C.c_uint32, C.c_uint32, C.c_int, i16p]),
             "llmx_run_token": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, i16p]),
             "llmx_lm_head_argmax_device": (C.c_int, [vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp]),
+            "llmx_upload_vocab": (C.c_int, [vp, vp]),
+            "llmx_generate": (C.c_int, [vp, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -367,6 +369,22 @@ class Accelerator:
     @property
     def device_bytes(self):
         return lib().llmx_device_bytes(self.h)
+
+    def upload_vocab(self, m: Model):
+        check(lib().llmx_upload_vocab(self.h, m.h), "upload_vocab")
+
+    def generate(self, prompt, max_new, block_rows=8, layer_count=0, last_block=False):
+        """Greedy generation on the device (host:9016-9132).  Returns the max_new
+        tokens, plus the last prompt block's final-normed rows if last_block."""
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.zeros(max(int(max_new), 1), np.uint32)
+        nlast = (len(p) - 1) % block_rows + 1 if len(p) else 0
+        rows = np.zeros((nlast, self.shape.hidden), np.int16) if last_block else None
+        check(lib().llmx_generate(self.h, p, len(p), block_rows, layer_count, max_new,
+                                  toks.ctypes.data_as(C.c_void_p),
+                                  rows.ctypes.data_as(C.c_void_p) if rows is not None else None), "generate")
+        toks = [int(t) for t in toks[:max_new]]
+        return (toks, rows) if last_block else toks
 
 
 class Executor:
