@@ -87,6 +87,10 @@ struct AttnArgs {
     int max_seq;
     int tpc_max;         // ceil(ceil(max_seq/64) / kCluster): tiles per CTA at most
     int32_t qk_scale;    // accum(fm(1/sqrt(hd))) raw, Q16.16
+    // Weights the next kernels stream (this layer's O, then Gate/Up), warmed into
+    // L2 while attention leaves HBM idle: pf_bytes (a multiple of 16) from pf.
+    const char *pf;
+    unsigned long long pf_bytes;
 };
 
 struct NormArgs {

@@ -78,6 +78,10 @@ struct llmx_ctx {
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
+    // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_kb
+    // KiB from the layer's O weights on (LLMX_ATTN_PREFETCH_KB / _ROWS; measured on
+    // B200: 28-32 MiB best, 64 MiB and more slower, no gain at 8 rows)
+    int attn_pf_kb = 28 * 1024, attn_pf_rows = 2;
     // fused one-row decode (stack.cu): plan, scratch, barrier counter
     bool fused = false;
     StackArgs stack{};
@@ -209,6 +213,9 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.max_seq = c->s.max_seq;
     t.tpc_max = c->tpc_max;
     t.qk_scale = c->qk_scale;
+    // O then Gate/Up follow the QKV words of the layer blob
+    t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
+    t.pf_bytes = std::min<unsigned long long>((c->w_o + c->w_gu) * 4ull, (unsigned long long)c->attn_pf_kb << 10);
     return t;
 }
 
@@ -271,7 +278,9 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         ProjArgs a = qkv_args(c, layer, in);
         set_stages(c, a, EPI_QKV, rt);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
-        CK(launch_attn(attn_args(c, layer), (int)rows, c->stream));
+        AttnArgs t = attn_args(c, layer);
+        if (rows > (uint32_t)c->attn_pf_rows) t.pf_bytes = 0;
+        CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
         set_stages(c, o, ge, rt);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
@@ -509,6 +518,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
     c->ring_wide_kb = env_int("LLMX_RING_WIDE_KB", 176, 8, 200);  // measured best for Down on B200
     c->ring_gu_kb = env_int("LLMX_RING_GU_KB", c->ring_kb, 8, 200);
+    c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 28 * 1024, 0, 1 << 20);
+    c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     auto bail = [&](int code) {
         release(c);
@@ -858,7 +869,11 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
             set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
-        case LLMX_KERNEL_ATTN: return launch_attn(attn_args(c, layer), (int)rows, c->stream);
+        case LLMX_KERNEL_ATTN: {
+            AttnArgs t = attn_args(c, layer);
+            if (rows > (uint32_t)c->attn_pf_rows) t.pf_bytes = 0;
+            return launch_attn(t, (int)rows, c->stream);
+        }
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
             o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
