@@ -40,18 +40,10 @@ namespace cg = cooperative_groups;
 constexpr int kKvStride = 136;  // padded smem row (int16): 272 B, 16-B aligned, conflict-free LDS.128
 constexpr int kAttnThreads = 256;
 constexpr int kMaxHd = 128;
-constexpr unsigned kPrefetchChunk = 64 * 1024;  // bytes per bulk L2 prefetch
 
 static __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-// Bulk L2 prefetch of [p, p + n): p 16-byte aligned, n a multiple of 16.
-static __device__ __forceinline__ void l2_prefetch(const char *p, unsigned long long n) {
-    for (unsigned long long b = 0; b < n; b += kPrefetchChunk) {
-        const unsigned c = (unsigned)min((unsigned long long)kPrefetchChunk, n - b);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + b), "r"(c) : "memory");
-    }
 }
 static __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
@@ -142,13 +134,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         for (int i = threadIdx.x; i < vpr; i += blockDim.x) reinterpret_cast<uint4 *>(m.q)[i] = qsrc[i];
     }
     for (int i = threadIdx.x; i < nown; i += blockDim.x) m.tsum[i] = 0;
-    if (threadIdx.x == 0 && a.pf_bytes) {  // this CTA's slice of the L2 warm-up
-        const unsigned long long nb = (unsigned long long)gridDim.x * gridDim.y;
-        const unsigned long long per = ((a.pf_bytes + nb - 1) / nb + 15) & ~15ull;
-        const unsigned long long b0 = (blockIdx.y * (unsigned long long)gridDim.x + blockIdx.x) * per;
-        const unsigned long long b1 = min(b0 + per, a.pf_bytes);
-        if (b0 < b1) l2_prefetch(a.pf + b0, b1 - b0);
-    }
+    if (threadIdx.x == 0 && a.pf_bytes && !a.pf_late)  // this CTA's slice of the L2 warm-up
+        l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     cp_async_wait_all();
     __syncthreads();
 
@@ -205,6 +192,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         }
     }
     cluster.sync();
+    if (threadIdx.x == 0 && a.pf_bytes && a.pf_late)
+        l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
 
     // ---- 2. running maxima, probabilities, tile sums, rescale, PV ----------
     // running max after tile t = prefix max of tile maxima, m_{-1} = fm(-128)

@@ -37,6 +37,19 @@ static __device__ __forceinline__ int64_t shfl_xor64(int64_t v, int o) {
 }
 
 
+// Bulk L2 prefetch (cp.async.bulk.prefetch.L2) of slice `part` of `parts` equal,
+// 16-byte aligned slices of [p, p + n): p 16-byte aligned, n a multiple of 16.
+constexpr unsigned kPrefetchChunk = 64 * 1024;  // bytes per prefetch instruction
+static __device__ __forceinline__ void l2_prefetch_slice(const char *p, unsigned long long n, unsigned part,
+                                                         unsigned parts) {
+    const unsigned long long per = ((n + parts - 1) / parts + 15) & ~15ull;
+    const unsigned long long b0 = part * per, b1 = min(b0 + per, n);
+    for (unsigned long long b = b0; b < b1; b += kPrefetchChunk) {
+        const unsigned c = (unsigned)min((unsigned long long)kPrefetchChunk, b1 - b);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + b), "r"(c) : "memory");
+    }
+}
+
 static __device__ __forceinline__ int32_t lo16(uint32_t w) { return (int32_t)(int16_t)(w & 0xffffu); }
 static __device__ __forceinline__ int32_t hi16(uint32_t w) { return (int32_t)(int16_t)(w >> 16); }
 // product of a Q8.8 (or raw Q2.14 payload) value and a Q4.12 value rounded to

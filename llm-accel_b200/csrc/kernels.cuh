@@ -91,6 +91,7 @@ struct AttnArgs {
     // L2 while attention leaves HBM idle: pf_bytes (a multiple of 16) from pf.
     const char *pf;
     unsigned long long pf_bytes;
+    int pf_late;         // issue it after the first cluster barrier (K and V in shared memory)
 };
 
 struct NormArgs {

@@ -82,6 +82,7 @@ struct llmx_ctx {
     // KiB from the layer's O weights on (LLMX_ATTN_PREFETCH_KB / _ROWS; measured on
     // B200: 28-32 MiB best, 64 MiB and more slower, no gain at 8 rows)
     int attn_pf_kb = 28 * 1024, attn_pf_rows = 2;
+    int attn_pf_late = 1;  // after attention's K/V loads (LLMX_ATTN_PREFETCH_LATE=0: at kernel start)
     // fused one-row decode (stack.cu): plan, scratch, barrier counter
     bool fused = false;
     StackArgs stack{};
@@ -216,6 +217,7 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     // O then Gate/Up follow the QKV words of the layer blob
     t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
     t.pf_bytes = std::min<unsigned long long>((c->w_o + c->w_gu) * 4ull, (unsigned long long)c->attn_pf_kb << 10);
+    t.pf_late = c->attn_pf_late;
     return t;
 }
 
@@ -520,6 +522,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->ring_gu_kb = env_int("LLMX_RING_GU_KB", c->ring_kb, 8, 200);
     c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 28 * 1024, 0, 1 << 20);
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
+    c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     auto bail = [&](int code) {
         release(c);
