@@ -134,8 +134,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         for (int i = threadIdx.x; i < vpr; i += blockDim.x) reinterpret_cast<uint4 *>(m.q)[i] = qsrc[i];
     }
     for (int i = threadIdx.x; i < nown; i += blockDim.x) m.tsum[i] = 0;
-    if (threadIdx.x == 0 && a.pf_bytes && !a.pf_late)  // this CTA's slice of the L2 warm-up
-        l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    // L2 warm-up: the same byte count in every CTA (from the step record), one slice each
+    const unsigned long long pf_n =
+        min(a.pf_bytes, a.pf_per_tile * (unsigned long long)((st.position + st.rows + kTile - 1) / kTile)) & ~15ull;
+    if (threadIdx.x == 0 && pf_n && !a.pf_late)
+        l2_prefetch_slice(a.pf, pf_n, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     cp_async_wait_all();
     __syncthreads();
 
@@ -192,8 +195,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         }
     }
     cluster.sync();
-    if (threadIdx.x == 0 && a.pf_bytes && a.pf_late)
-        l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    if (threadIdx.x == 0 && pf_n && a.pf_late)
+        l2_prefetch_slice(a.pf, pf_n, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
 
     // ---- 2. running maxima, probabilities, tile sums, rescale, PV ----------
     // running max after tile t = prefix max of tile maxima, m_{-1} = fm(-128)

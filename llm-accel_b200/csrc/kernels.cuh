@@ -88,9 +88,12 @@ struct AttnArgs {
     int tpc_max;         // ceil(ceil(max_seq/64) / kCluster): tiles per CTA at most
     int32_t qk_scale;    // accum(fm(1/sqrt(hd))) raw, Q16.16
     // Weights the next kernels stream (this layer's O, then Gate/Up), warmed into
-    // L2 while attention leaves HBM idle: pf_bytes (a multiple of 16) from pf.
+    // L2 while attention leaves HBM idle: pf_per_tile bytes per 64-position tile
+    // of the longest row's context (attention time grows with it), at most
+    // pf_bytes, from pf; all multiples of 16.
     const char *pf;
     unsigned long long pf_bytes;
+    unsigned long long pf_per_tile;
     int pf_late;         // issue it after the first cluster barrier (K and V in shared memory)
 };
 

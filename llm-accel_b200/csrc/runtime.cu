@@ -78,10 +78,12 @@ struct llmx_ctx {
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
-    // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_kb
-    // KiB from the layer's O weights on (LLMX_ATTN_PREFETCH_KB / _ROWS; measured on
-    // B200: 28-32 MiB best, 64 MiB and more slower, no gain at 8 rows)
-    int attn_pf_kb = 28 * 1024, attn_pf_rows = 2;
+    // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_tile_kb
+    // KiB per 64-position context tile from the layer's O weights on, at most
+    // attn_pf_kb KiB and the end of Gate/Up (LLMX_ATTN_PREFETCH_TILE_KB, _KB, _ROWS).
+    // Measured on B200: ~33 MiB best at context ~600, ~70 MiB at ~2200 (98 MiB
+    // slower); no gain at 8 rows.
+    int attn_pf_tile_kb = 3584, attn_pf_kb = 72 * 1024, attn_pf_rows = 2;
     int attn_pf_late = 1;  // after attention's K/V loads (LLMX_ATTN_PREFETCH_LATE=0: at kernel start)
     // fused one-row decode (stack.cu): plan, scratch, barrier counter
     bool fused = false;
@@ -216,7 +218,9 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.qk_scale = c->qk_scale;
     // O then Gate/Up follow the QKV words of the layer blob
     t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
-    t.pf_bytes = std::min<unsigned long long>((c->w_o + c->w_gu) * 4ull, (unsigned long long)c->attn_pf_kb << 10);
+    t.pf_bytes = (c->w_o + c->w_gu) * 4ull;
+    if (c->attn_pf_kb) t.pf_bytes = std::min<unsigned long long>(t.pf_bytes, (unsigned long long)c->attn_pf_kb << 10);
+    t.pf_per_tile = (unsigned long long)c->attn_pf_tile_kb << 10;
     t.pf_late = c->attn_pf_late;
     return t;
 }
@@ -281,7 +285,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         set_stages(c, a, EPI_QKV, rt);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         AttnArgs t = attn_args(c, layer);
-        if (rows > (uint32_t)c->attn_pf_rows) t.pf_bytes = 0;
+        if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
         CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
         set_stages(c, o, ge, rt);
@@ -520,7 +524,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
     c->ring_wide_kb = env_int("LLMX_RING_WIDE_KB", 176, 8, 200);  // measured best for Down on B200
     c->ring_gu_kb = env_int("LLMX_RING_GU_KB", c->ring_kb, 8, 200);
-    c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 28 * 1024, 0, 1 << 20);
+    c->attn_pf_tile_kb = env_int("LLMX_ATTN_PREFETCH_TILE_KB", 3584, 0, 1 << 20);
+    c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 72 * 1024, 0, 1 << 22);
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
@@ -874,7 +879,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         }
         case LLMX_KERNEL_ATTN: {
             AttnArgs t = attn_args(c, layer);
-            if (rows > (uint32_t)c->attn_pf_rows) t.pf_bytes = 0;
+            if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
             return launch_attn(t, (int)rows, c->stream);
         }
         case LLMX_KERNEL_O: {
