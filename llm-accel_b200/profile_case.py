@@ -5,7 +5,9 @@ weights), preloads a seeded KV cache to `--position`, then
   --table : prints the mean device time of every kernel (llmx_time_kernel,
             CUDA events on the context stream) for 1-row decode and 8-row blocks;
   --eager : runs `--steps` eager Task 18/19/20 sequences (no CUDA graph) so that a
-            profiler sees plain launches (ncu -k regex:... -c ...).
+            profiler sees plain launches (ncu -k regex:... -c ...);
+  --argmax: runs `--steps` device LM-head argmaxes over a 151,936 x 2048 table
+            (k_lm_scan + k_lm_pick) and prints their mean device time.
 Usage: python llm-accel_b200/profile_case.py --layers 4 --position 512 --table
 """
 from __future__ import annotations
@@ -33,7 +35,10 @@ def main():
     ap.add_argument("--rows", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--iters", type=int, default=40)
+    ap.add_argument("--argmax", action="store_true")
     args = ap.parse_args()
+    if args.argmax:
+        return argmax_case(args.steps)
     s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq)
     m = llmx.Model(s).init_gaussian(20260718, 0.02)
     acc = llmx.Accelerator(s)
@@ -62,6 +67,31 @@ def main():
             acc.task(llmx.OP_FINAL_NORM, 0, pos, args.rows)
         print("eager steps done")
     acc.close()
+
+
+def argmax_case(steps):
+    import torch
+    s = llmx.shape("qwen2.5-3b", layers=1)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(1)
+    w = torch.randint(-700, 700, (s.vocab, s.hidden), dtype=torch.int16, device=dev, generator=g)
+    h = torch.randint(-2000, 2000, (1, s.hidden), dtype=torch.int16, device=dev, generator=g)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run():
+        llmx.lm_head_argmax_device(h.data_ptr(), 1, s.hidden, w.data_ptr(), s.vocab, tok.data_ptr(),
+                                   stream.cuda_stream)
+    run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    print(json.dumps({"lm_head_argmax_us": ms * 1e3, "gbs": s.vocab * s.hidden * 2 / (ms * 1e-3) / 1e9,
+                      "token": int(tok.item())}))
 
 
 if __name__ == "__main__":
