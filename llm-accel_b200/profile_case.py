@@ -36,6 +36,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--argmax", action="store_true")
+    ap.add_argument("--kv-scale", type=float, default=600.0, help="std of the preloaded KV cache (raw Q8.8)")
     args = ap.parse_args()
     if args.argmax:
         return argmax_case(args.steps)
@@ -46,8 +47,8 @@ def main():
     rng = np.random.default_rng(0)
     P = args.position
     for l in range(s.layers):
-        k = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
-        v = np.clip(rng.normal(0, 600, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
+        k = np.clip(rng.normal(0, args.kv_scale, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
+        v = np.clip(rng.normal(0, args.kv_scale, (s.kv_heads, P, s.head_dim)), -32768, 32767).astype(np.int16)
         acc.write_kv(l, 0, k, v)
     acc.write_hidden(1, m.embed(rng.integers(0, s.vocab, 8)))
     if args.table:
