@@ -11,7 +11,8 @@
 // (sum, acc) update is sequential: the running max after tile t is the prefix
 // max of tile maxima, and a tile's probabilities / PV only need that value.
 //
-// One thread-block cluster of kCluster CTAs handles one (row, query head).
+// One thread-block cluster of C CTAs (8, or 16 when few heads leave SMs idle)
+// handles one (row, query head).
 // CTA c owns the contiguous tiles [c*tpc, (c+1)*tpc):
 //   1. K rows of its tiles land in shared memory (cp.async); QK scores of its
 //      positions; the buffer is refilled with the V rows while each owned
@@ -21,7 +22,7 @@
 //      CTA) and the raw-payload PV tile values, each pushed to the CTA that
 //      finalises that output element;
 //   3. cluster barrier; the (sum, acc) recurrence in tile order on local
-//      shared memory, each CTA finalising hd/kCluster output elements.
+//      shared memory, each CTA finalising hd/C output elements.
 // All remote accesses are stores issued before a barrier, so after each
 // barrier a CTA reads only its own shared memory, and no CTA needs to wait for
 // the others before it exits.  All waits are hardware cluster barriers: no
@@ -56,7 +57,7 @@ struct AttnSmem {      // carved out of dynamic shared memory
     int16_t *ptab;     // [2049] softmax exp table
     int16_t *q;        // [hd]
     int16_t *sc;       // [tpc*64] scores, then Q2.14 probabilities
-    int16_t *tvr;      // [kMaxTiles][hd/kCluster] tile values of the elements this CTA finalises
+    int16_t *tvr;      // [kMaxTiles][hd/C] tile values of the elements this CTA finalises
     int32_t *mloc;     // [kMaxTiles] every tile's maximum (pushed by the owners)
     int32_t *gsum;     // [kMaxTiles] every tile's sum (pushed)
     int32_t *gold;     // [kMaxTiles] every tile's rescale factor (pushed)
@@ -65,14 +66,14 @@ struct AttnSmem {      // carved out of dynamic shared memory
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, size_t off[9]) {
+static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[9]) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
     off[0] = b; b = align16(b + rows * kKvStride * 2);                       // kv
     off[1] = b; b = align16(b + 2049 * 2);                                   // ptab
     off[2] = b; b = align16(b + (size_t)kMaxHd * 2);                         // q
     off[3] = b; b = align16(b + rows * 2);                                   // sc
-    off[4] = b; b = align16(b + (size_t)kMaxTiles * (kMaxHd / kCluster) * 2); // tvr
+    off[4] = b; b = align16(b + (size_t)kMaxTiles * (kMaxHd / cl) * 2);      // tvr
     off[5] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // mloc
     off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
     off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
@@ -81,21 +82,22 @@ static __host__ __device__ size_t attn_layout(int tpc, int hd, size_t off[9]) {
     return b;
 }
 
-size_t attn_smem_bytes(int tpc, int hd) {
+size_t attn_smem_bytes(int tpc, int hd, int cluster) {
     size_t off[9];
-    return attn_layout(tpc, hd, off);
+    return attn_layout(tpc, hd, cluster, off);
 }
 
 
+template <int C>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     extern __shared__ __align__(16) char raw[];
     cg::cluster_group cluster = cg::this_cluster();
     const int c = (int)cluster.block_rank();
-    const int lh = blockIdx.x / kCluster;  // local query head
+    const int lh = blockIdx.x / C;  // local query head
     const int r = blockIdx.y;
-    const int hd = a.hd, vpr = hd >> 3, epc = hd / kCluster;  // elements finalised per CTA
+    const int hd = a.hd, vpr = hd >> 3, epc = hd / C;  // elements finalised per CTA
     size_t off[9];
-    attn_layout(a.tpc_max, hd, off);
+    attn_layout(a.tpc_max, hd, C, off);
     AttnSmem m;
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
     m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const bool row_ok = r < st.rows;
     const int ctx = st.position + r + 1;
     const int ntiles = row_ok ? (ctx + kTile - 1) / kTile : 0;
-    const int tpc = max(1, (ntiles + kCluster - 1) / kCluster);
+    const int tpc = max(1, (ntiles + C - 1) / C);
     const int t_begin = min(c * tpc, ntiles), t_end = min(t_begin + tpc, ntiles);
     const int nown = t_end - t_begin;
     const int p_begin = t_begin * kTile;
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
             for (int j = lane; j < pe; j += 32) mx = max(mx, (int32_t)m.sc[tl * kTile + j]);
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane < kCluster) *cluster.map_shared_rank(m.mloc + t_begin + tl, lane) = mx;
+            if (lane < C) *cluster.map_shared_rank(m.mloc + t_begin + tl, lane) = mx;
         }
     }
     cluster.sync();
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         int32_t d = sat16(mprev - mt);
         d = d < -2048 ? -2048 : d;
         const int32_t old = m.ptab[d + 2048];
-        for (int k = 0; k < kCluster; k++) {
+        for (int k = 0; k < C; k++) {
             *cluster.map_shared_rank(m.gsum + t, k) = m.tsum[i];
             *cluster.map_shared_rank(m.gold + t, k) = old;
         }
@@ -245,13 +247,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
         ts = sat32(rnd((int64_t)ts * 1024, 16));
         const int16_t tv = (int16_t)sat16(rnd(ts, 8));
-        *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / kCluster, e % kCluster) = tv;
+        *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
     }
     cluster.sync();
 
     // ---- 3. in-order Q16.16 recurrence on local shared memory ---------------
     for (int j = threadIdx.x; ntiles > 0 && j < epc; j += blockDim.x) {
-        const int e = j * kCluster + c;
+        const int e = j * C + c;
         int32_t sum = 0, acc = 0;
         for (int u = 0; u < ntiles; u++) {
             const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
@@ -264,28 +266,34 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     }
 }
 
-cudaError_t attn_configure(int max_smem_bytes) {
-    return cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+cudaError_t attn_configure(int max_smem_bytes, int cluster) {
+    if (cluster == kClusterWide) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn<kClusterWide>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        return cudaFuncSetAttribute(k_attn<kClusterWide>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+    }
+    return cudaFuncSetAttribute(k_attn<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
 }
 
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     AttnArgs c = a;
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kCluster * a.q_heads, rows);
+    cfg.gridDim = dim3(a.cluster * a.q_heads, rows);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd);
+    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = kCluster;
+    attr[1].val.clusterDim.x = a.cluster;
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelExC(&cfg, (const void *)k_attn, args);
+    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn<kClusterWide> : (const void *)k_attn<kCluster>;
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 }  // namespace llmx

@@ -70,7 +70,11 @@ struct ProjArgs {
     int row0;            // first row of this launch (x / out / resid already offset)
 };
 
-constexpr int kCluster = 8;         // CTAs per (row, query head) attention cluster
+// CTAs per (row, query head) attention cluster: 8, or 16 (a non-portable size
+// B200 supports) when few heads leave most SMs idle, so that the contexts
+// longer than 16 tiles are spread 3 tiles per CTA instead of 5.
+constexpr int kCluster = 8;
+constexpr int kClusterWide = 16;
 constexpr int kMaxTilesPerCta = 5;  // bounds the cluster's shared memory: max_seq <= 2560
 
 struct AttnArgs {
@@ -85,7 +89,8 @@ struct AttnArgs {
     int gqa;             // query heads per KV head (model)
     int hd;
     int max_seq;
-    int tpc_max;         // ceil(ceil(max_seq/64) / kCluster): tiles per CTA at most
+    int cluster;         // CTAs per cluster (kCluster or kClusterWide)
+    int tpc_max;         // ceil(ceil(max_seq/64) / cluster): tiles per CTA at most
     int32_t qk_scale;    // accum(fm(1/sqrt(hd))) raw, Q16.16
     // Weights the next kernels stream (this layer's O, then Gate/Up), warmed into
     // L2 while attention leaves HBM idle: pf_per_tile bytes per 64-position tile
@@ -127,8 +132,8 @@ cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 // Launchers (stream-ordered, programmatic-dependent launch enabled).
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s);
-cudaError_t attn_configure(int max_smem_bytes);
-size_t attn_smem_bytes(int tpc, int hd);
+cudaError_t attn_configure(int max_smem_bytes, int cluster);
+size_t attn_smem_bytes(int tpc, int hd, int cluster);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 cudaError_t proj_configure(int max_smem_bytes);

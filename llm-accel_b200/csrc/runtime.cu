@@ -65,6 +65,11 @@ struct llmx_ctx {
     cudaStream_t stream = nullptr;
     // geometry of this rank
     int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, tpc_max = 0;
+    // 16-CTA attention clusters when rows x local heads x 16 CTAs fill at most half of
+    // the SMs and the context can exceed 16 tiles (tensor-parallel ranks of 4 or 2
+    // heads; measured at context 2049: 14.5 -> 11.0 us, no gain at 8 heads)
+    int tpc_max_wide = 0;
+    bool attn_wide = false;
     // weights: per layer [QKV | O | GU | D] words
     size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
     uint32_t *wbuf = nullptr;
@@ -215,6 +220,7 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.hd = c->hd;
     t.max_seq = c->s.max_seq;
     t.tpc_max = c->tpc_max;
+    t.cluster = kCluster;
     t.qk_scale = c->qk_scale;
     // O then Gate/Up follow the QKV words of the layer blob
     t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
@@ -223,6 +229,14 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.pf_per_tile = (unsigned long long)c->attn_pf_tile_kb << 10;
     t.pf_late = c->attn_pf_late;
     return t;
+}
+
+// Cluster size of an attention launch of `rows` rows.
+void pick_attn_cluster(const llmx_ctx *c, AttnArgs &t, uint32_t rows) {
+    if (c->attn_wide && 2 * (int)rows * c->hq * kClusterWide <= c->nsm) {
+        t.cluster = kClusterWide;
+        t.tpc_max = c->tpc_max_wide;
+    }
 }
 
 ProjArgs o_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in) {
@@ -285,6 +299,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         set_stages(c, a, EPI_QKV, rt);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         AttnArgs t = attn_args(c, layer);
+        pick_attn_cluster(c, t, rows);
         if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
         CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
@@ -519,7 +534,9 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->Hq = hq * hd;
     c->Il = s.inter / tp_size;
     c->c0 = tp_rank * c->Il;
-    c->tpc_max = ((s.max_seq + kTile - 1) / kTile + kCluster - 1) / kCluster;
+    const int max_tiles = (s.max_seq + kTile - 1) / kTile;
+    c->tpc_max = (max_tiles + kCluster - 1) / kCluster;
+    c->tpc_max_wide = (max_tiles + kClusterWide - 1) / kClusterWide;
     c->layer_loaded.assign(s.layers, false);
     c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
     c->ring_wide_kb = env_int("LLMX_RING_WIDE_KB", 176, 8, 200);  // measured best for Down on B200
@@ -543,8 +560,15 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
     e = proj_configure(kProjSmem);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
-    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd));
+    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
+    // LLMX_ATTN_WIDE=0 keeps 8-CTA clusters everywhere
+    if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && 2 * c->hq * kClusterWide <= c->nsm &&
+        env_int("LLMX_ATTN_WIDE", 1, 0, 1) == 1) {
+        e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide), kClusterWide);
+        if (e == cudaSuccess) c->attn_wide = true;
+        else (void)cudaGetLastError();  // keep 8-CTA clusters
+    }
 
     const size_t H = s.hidden;
     c->w_qkv = (size_t)(c->Hq + 2 * c->KV) * H / 2;
@@ -879,6 +903,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         }
         case LLMX_KERNEL_ATTN: {
             AttnArgs t = attn_args(c, layer);
+            pick_attn_cluster(c, t, rows);
             if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
             return launch_attn(t, (int)rows, c->stream);
         }

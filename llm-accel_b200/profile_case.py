@@ -37,10 +37,16 @@ def main():
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--argmax", action="store_true")
     ap.add_argument("--kv-scale", type=float, default=600.0, help="std of the preloaded KV cache (raw Q8.8)")
+    ap.add_argument("--hidden", type=int, default=0, help="override the shape (e.g. a tensor-parallel rank's heads)")
+    ap.add_argument("--heads", type=int, default=0)
+    ap.add_argument("--kv-heads", type=int, default=0)
+    ap.add_argument("--inter", type=int, default=0)
     args = ap.parse_args()
     if args.argmax:
         return argmax_case(args.steps)
-    s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq)
+    over = {k: v for k, v in (("hidden", args.hidden), ("heads", args.heads), ("kv_heads", args.kv_heads),
+                              ("inter", args.inter)) if v}
+    s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq, **over)
     m = llmx.Model(s).init_gaussian(20260718, 0.02)
     acc = llmx.Accelerator(s)
     acc.upload_model(m)

@@ -144,6 +144,40 @@ def test_long_context_gaussian(llmx, oracle):
     acc.close()
 
 
+@pytest.mark.parametrize("heads,kv_heads,hidden", [(4, 1, 512), (2, 1, 256)])
+def test_long_context_few_heads(llmx, oracle, monkeypatch, heads, kv_heads, hidden):
+    """A layer with as few query heads as a tensor-parallel rank holds (4 / 2):
+    one-row decodes at contexts above 16 tiles run 16-CTA attention clusters
+    (3 tiles per CTA); the same rows with 8-CTA clusters (LLMX_ATTN_WIDE=0) and
+    the oracle must agree."""
+    s = llmx.shape("qwen-layer-long", hidden=hidden, heads=heads, kv_heads=kv_heads, inter=hidden * 2 + 256)
+    m = llmx.Model(s).init_gaussian(20260718 + heads, 0.02)
+    wide = llmx.Accelerator(s)
+    monkeypatch.setenv("LLMX_ATTN_WIDE", "0")
+    narrow = llmx.Accelerator(s)
+    monkeypatch.delenv("LLMX_ATTN_WIDE")
+    ref = OracleState(oracle, oracle_shape(oracle, s), [m.layer(0)], m.norms())
+    rng = np.random.default_rng(heads)
+    P = 1900
+    k, v = random_kv(rng, s.kv_heads, P, s.head_dim)
+    ref.kc[0][:, :P] = k
+    ref.vc[0][:, :P] = v
+    for acc in (wide, narrow):
+        acc.upload_model(m)
+        acc.write_kv(0, 0, k, v)
+    h = m.embed(rng.integers(0, s.vocab, 8))
+    want = ref.stack(h, P)
+    for acc, what in ((wide, "wide"), (narrow, "narrow")):
+        _assert_same(acc.stack(h, position=P), want, f"block at {P} ({what})")
+    for pos in (1919, 1983, 1984, 2047):
+        d = m.embed([int(rng.integers(0, s.vocab))])
+        want = ref.stack(d, pos)
+        for acc, what in ((wide, "wide"), (narrow, "narrow")):
+            _assert_same(acc.stack(d, position=pos), want, f"decode at {pos} ({what})")
+    wide.close()
+    narrow.close()
+
+
 def test_status_and_errors_on_device(llmx, small):
     """Controller status codes (include/control_cache_8x64.hpp:279-286) from
     the device entry point: bad rows / operator / layer / position."""
