@@ -227,8 +227,10 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
     gpu_launches = launches[0]
     clock = clocks.stop()
 
-    # end to end through the public API: host embedding rows in pinned memory,
-    # H2D, the stack, final norm, D2H of the output row, every step
+    # end to end through the public API: the step's embedding row copied from the
+    # host table (rows, drawn before timing -- a resident table as in
+    # model_data_t::embedding host:871-884) into pinned memory, H2D, the stack,
+    # final norm, D2H of the output row, every step
     in_p = torch.empty((1, H), dtype=torch.int16).pin_memory()
     out_p = torch.empty((1, H), dtype=torch.int16).pin_memory()
     in_np = in_p.numpy()
@@ -236,7 +238,7 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
 
     def e2e():
         for i in range(K):
-            in_np[0] = embed_rows([dec[i]], H)[0] if model is None else model.embed([dec[i]])[0]
+            in_np[0] = rows[P + i]
             acc.stack_raw(in_p.data_ptr(), 1, 0, L, P + i, True, out_p.data_ptr())
             if len(e2e_outputs) < 8:
                 e2e_outputs.append(out_p.numpy().copy())
@@ -293,7 +295,7 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
                      "ms_per_launch": gu_ms, "down_ms_per_launch": down_ms, "peak_source": peak_kind},
         "e2e": {"value": K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
                 "d2h_bytes_per_step": H * 2, "wall_ms_per_step": e2e_wall_ms / K,
-                "api": "llmx_stack (run_token boundary: host embedding row -> H2D -> 36x Task18/19 -> Task20 -> D2H)"},
+                "api": "llmx_stack (run_token boundary: host embedding-table row -> H2D -> 36x Task18/19 -> Task20 -> D2H)"},
         "gpu_launches": gpu_launches,
         "clocks": clock,
         "setup_s": setup_s,
