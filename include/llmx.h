@@ -212,6 +212,22 @@ void *llmx_hidden_device_ptr(llmx_ctx *ctx, uint32_t pair);
 uint64_t llmx_kernel_launches(const llmx_ctx *ctx);
 /* Bytes of device memory the context holds. */
 uint64_t llmx_device_bytes(const llmx_ctx *ctx);
+/* How a tensor-parallel context adds the ranks' exact partial sums after the
+ * O and Down projections (no reference counterpart: the reference runs on one
+ * device; this is the all-reduce of the tensor-parallel split).  Every rank of
+ * a group reports the same kind: the ranks agree on it in llmx_create. */
+#define LLMX_AR_NONE 0   /* one GPU: no all-reduce */
+#define LLMX_AR_NCCL 1   /* ncclAllReduce(int64) + rounding kernel (LLMX_TP_NCCL=1, or some rank
+                            could not map a peer's exchange region) */
+#define LLMX_AR_PEER 2   /* peer stores over NVLink, finished in the next projection's prologue */
+int llmx_allreduce_kind(const llmx_ctx *ctx);
+/* Failure-detection self-test (no reference counterpart; the reference's
+ * controller has no waits that can expire).  Runs the receiving side of the
+ * peer all-reduce on an exchange region that no rank writes, with a wait of
+ * at most poll_limit polls per word: the kernel gives up, records its error
+ * status and returns, and the call returns LLMX_ERR_TIMEOUT with the context
+ * still usable.  Works on one GPU; overwrites hidden pair 0. */
+int llmx_selftest_ar_timeout(llmx_ctx *ctx, uint32_t poll_limit);
 
 /* Kernels of the path, for per-kernel timing (no reference counterpart: the
  * reference reads its CU running times from the XRT profile_kernels.csv,
@@ -248,6 +264,8 @@ int llmx_time_kernel(llmx_ctx *ctx, int kernel, uint32_t layer, uint32_t positio
  * Limits: 1 <= rows <= 8 (LLMX_ERR_ARG beyond), hidden_size a multiple of 8.
  * The first call on each device does a one-time set-up there (looks up the
  * scratch array's address); make that first call before any stream capture.
+ * The address is kept for the life of the process, so do not call this after
+ * cudaDeviceReset() on a device it has already been used on.
  * Calls share the scratch, so calls that may overlap on the device (different
  * streams without ordering) race: order them on one stream or with events.
  * Stream-ordered: returns after enqueueing two kernels. */

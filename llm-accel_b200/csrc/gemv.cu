@@ -41,11 +41,104 @@ struct Warps {
 // when a norm row is given (stream_rmsnorm kernel/compute_stream.cpp:227-288).
 constexpr int kStageBatch = 4;  // 16-byte activation loads in flight per thread while staging
 
+// Rows of a peer all-reduce -> shared memory (raw, before any norm): each
+// element waits for every rank's exact sum, x = sat16(resid + round(sum)).
+// Block 0 also writes the rows to in.hid_out: they are the residual of the next
+// sublayer (the output feature pair of the finished coarse task).
 template <int R>
-static __device__ void stage_rows(const ProjArgs &a, int16_t *xs, int rows, int tid) {
+static __device__ void stage_rows_allreduce(const ProjArgs &a, const Step &st, int16_t *xs, int rows, int tid) {
+    const int T = blockDim.x - 32, K = a.K;
+    const ArInput &in = a.in;
+    const uint32_t n = st.ar_base + in.ar_off;
+    const int slot = (int)(n & 1u);
+    const uint32_t tag = ar_tag(n);
+    __shared__ int fail_s;
+    if (tid == 0) fail_s = 0;
+    consumer_sync();
+    for (int i = tid; i < R * K; i += T) {
+        const int r = i / K, e = i - r * K;
+        int16_t x = 0;
+        if (r < rows) {
+            int64_t sum;
+            if (!ar_gather(in.ar, slot, tag, r, e, &fail_s, sum)) {
+                if (!fail_s) atomicCAS(a.error, 0, kErrArTimeout);
+                fail_s = 1;
+                sum = 0;
+            }
+            x = (int16_t)sat16((int32_t)in.resid[i] + round_mac(sum));
+            if (blockIdx.x == 0) in.hid_out[i] = x;
+        }
+        xs[i] = x;
+    }
+    consumer_sync();
+}
+
+// In-place RMSNorm of rows already staged in shared memory (all-reduce input).
+template <int R>
+static __device__ void norm_rows_smem(const ProjArgs &a, int16_t *xs, int rows, int tid) {
+    constexpr int CW = Warps<R>::kConsumers;
+    const int T = blockDim.x - 32, cw = T / 32;
+    const int K = a.K, KV8 = K >> 3;
+    __shared__ int32_t inv_rms_s[kMaxRows];
+    if (a.inv_elems == 0) {
+        if (tid < R) inv_rms_s[tid] = a.inv_rms_const;
+    } else {
+        __shared__ int64_t red[CW][kMaxRows];
+        int64_t part[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) part[r] = 0;
+        for (int i = tid; i < K; i += T) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int32_t v = xs[r * K + i];
+                part[r] += (int64_t)v * v;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) part[r] += shfl_xor64(part[r], o);
+        if ((tid & 31) == 0)
+#pragma unroll
+            for (int r = 0; r < R; r++) red[tid >> 5][r] = part[r];
+        consumer_sync();
+        if (tid < R) {
+            int64_t sum = 0;
+            for (int w = 0; w < cw; w++) sum += red[w][tid];
+            inv_rms_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
+        }
+    }
+    consumer_sync();
+    uint4 *x4 = reinterpret_cast<uint4 *>(xs);
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(a.norm);
+    for (int i = tid; i < R * KV8; i += T) {
+        const int r = i / KV8, v = i - r * KV8;
+        const uint4 xv = x4[i], wv = w4[v];
+        const int64_t inv = r < rows ? inv_rms_s[r] : 0;
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int32_t y0 = sat16(rnd((int64_t)lo16(xw[q]) * inv * lo16(ww[q]), 16));
+            const int32_t y1 = sat16(rnd((int64_t)hi16(xw[q]) * inv * hi16(ww[q]), 16));
+            ow[q] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+        }
+        x4[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    consumer_sync();
+}
+
+template <int R>
+static __device__ void stage_rows(const ProjArgs &a, const Step &st, int16_t *xs, int rows, int tid) {
     constexpr int CW = Warps<R>::kConsumers;  // upper bound of the consumer warps
     const int T = blockDim.x - 32, cw = T / 32;
     const int K = a.K, KV8 = K >> 3;
+    if (a.in.ar.n > 1) {  // tensor parallel: the previous projection's all-reduce, finished here
+        stage_rows_allreduce<R>(a, st, xs, rows, tid);
+        if (a.norm != nullptr) norm_rows_smem<R>(a, xs, rows, tid);
+        return;
+    }
     __shared__ int32_t inv_rms_s[kMaxRows];
     if (a.norm != nullptr) {
         if (a.inv_elems == 0) {
@@ -221,10 +314,8 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     pdl_trigger();
     const Step st = *a.step;
     const int rows = st.rows - a.row0;  // rows of this launch (a block may be split in row groups)
-    const int ar_epoch = (EPI == EPI_PARTIAL && a.ar.n > 1) ? *a.ar.epoch : 0;
-    const int ar_slot = ar_epoch & 1;
-    const uint32_t ar_tag = (uint32_t)ar_epoch + 1u;
-    stage_rows<R>(a, xs, rows, tid);
+    const uint32_t ar_n = st.ar_base + a.ar_off;  // EPI_PARTIAL: this projection's all-reduce
+    stage_rows<R>(a, st, xs, rows, tid);
     const uint4 *xs4 = reinterpret_cast<const uint4 *>(xs);
     uint4 xr[8];  // 1-row decode with K <= 2048: this lane's activation vectors stay in registers
     if (R == 1 && VPL > 0 && VPL <= 8) {
@@ -312,15 +403,10 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
             if ((lane & (32 / N - 1)) != 0 || r >= rows) continue;
             if (EPI == EPI_PARTIAL) {
                 if (a.ar.n > 1) {  // straight into every rank's exchange region (NVLink stores)
-                    const size_t off = kArHeader + ((((size_t)ar_slot * kMaxTp + a.ar.me) * kMaxRows + r) *
-                                                    a.ar.hidden + unit) * 2 * sizeof(uint64_t);
-                    const uint64_t t = (uint64_t)ar_tag << 32;
-                    const uint64_t w0 = t | (uint32_t)(uint64_t)tot, w1 = t | (uint32_t)((uint64_t)tot >> 32);
-                    for (int p = 0; p < a.ar.n; p++) {
-                        uint64_t *d = reinterpret_cast<uint64_t *>(a.ar.base[p] + off);
-                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(w0) : "memory");
-                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d + 1), "l"(w1) : "memory");
-                    }
+                    const size_t w = ar_word_index((int)(ar_n & 1u), a.ar.me, r, a.ar.hidden, unit);
+                    const uint64_t word = ar_pack(tot, ar_tag(ar_n));
+                    for (int p = 0; p < a.ar.n; p++)
+                        ar_store(reinterpret_cast<uint64_t *>(a.ar.base[p] + kArHeader) + w, word);
                 } else {
                     a.partial[(size_t)r * a.out_stride + unit] = tot;
                 }

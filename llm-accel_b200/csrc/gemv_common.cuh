@@ -71,6 +71,44 @@ static __device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src,
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// ---- peer all-reduce words (layout and tags: ArPeers in kernels.cuh) -------
+static __device__ __forceinline__ uint64_t ar_pack(int64_t sum, uint32_t tag) {
+    return ((uint64_t)sum << 16) | (tag & 0xffffu);
+}
+static __device__ __forceinline__ int64_t ar_value(uint64_t w) { return (int64_t)w >> 16; }
+static __device__ __forceinline__ void ar_store(uint64_t *p, uint64_t w) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+static __device__ __forceinline__ uint64_t ar_load(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Exact sum of element (r, e) over every rank's contribution to all-reduce
+// (slot, tag), read from this rank's exchange region.  Each word is waited for
+// at most ar.poll_limit polls; false when one did not arrive (or when *fail was
+// set by another thread of the block, so that a block gives up once).
+static __device__ __forceinline__ bool ar_gather(const ArPeers &ar, int slot, uint32_t tag, int r, int e,
+                                                 const volatile int *fail, int64_t &sum) {
+    const uint64_t *words = reinterpret_cast<const uint64_t *>(ar.base[ar.me] + kArHeader);
+    uint64_t w[kMaxTp];
+#pragma unroll
+    for (int p = 0; p < kMaxTp; p++)
+        if (p < ar.n) w[p] = ar_load(words + ar_word_index(slot, p, r, ar.hidden, e));
+    sum = 0;
+#pragma unroll
+    for (int p = 0; p < kMaxTp; p++) {
+        if (p >= ar.n) break;
+        for (uint32_t it = 0; (uint32_t)(w[p] & 0xffffu) != tag; it++) {
+            if (it >= ar.poll_limit || *fail) return false;
+            __nanosleep(64);
+            w[p] = ar_load(words + ar_word_index(slot, p, r, ar.hidden, e));
+        }
+        sum += ar_value(w[p]);
+    }
+    return true;
+}
+
 // Named barrier over the consumer warps (the producer warp is the last warp).
 static __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x - 32) : "memory");

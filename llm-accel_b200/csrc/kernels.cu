@@ -7,6 +7,7 @@
 #include "device_util.cuh"
 #include "fixed.cuh"
 #include "kernels.cuh"
+#include "gemv_common.cuh"
 
 namespace llmx {
 
@@ -72,54 +73,35 @@ __global__ void k_round_resid(const ResidArgs a) {
         a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(a.partial[i]));
 }
 
-// Peer all-reduce, receiving side (one CTA): every thread polls the tagged
-// words of its elements from every rank (bounded), adds the ranks' exact sums
-// (order-free), rounds as round_mac and adds the residual -- the same result on
-// every rank.  The CTA then counts the all-reduce as done.
-__global__ void __launch_bounds__(1024) k_ar_finish(const ArFinishArgs a) {
+// Peer all-reduce, receiving side, as a kernel of its own (single coarse
+// tasks and the end of a stack; inside a stack the next projection's prologue
+// does this): every thread waits (bounded) for the words of one element from
+// every rank, adds the ranks' exact sums (order-free), rounds as round_mac and
+// adds the residual -- the same result on every rank.
+__global__ void __launch_bounds__(256) k_ar_finish(const ArFinishArgs a) {
     pdl_wait();
     pdl_trigger();
     __shared__ int fail_s;
     if (threadIdx.x == 0) fail_s = 0;
     __syncthreads();
-    const int epoch = *a.ar.epoch, slot = epoch & 1;
-    const uint32_t tag = (uint32_t)epoch + 1u;
-    const int rows = a.step->rows, H = a.ar.hidden;
-    const uint64_t *words = reinterpret_cast<const uint64_t *>(a.ar.base[a.ar.me] + kArHeader) +
-                            (size_t)slot * kMaxTp * kMaxRows * H * 2;
-    for (int i = threadIdx.x; i < rows * H; i += blockDim.x) {
-        int64_t sum = 0;
-        bool ok = true;
-        for (int p = 0; p < a.ar.n && ok; p++) {
-            const uint64_t *w = words + ((size_t)p * kMaxRows * H + i) * 2;
-            uint64_t w0 = 0, w1 = 0;
-            for (uint32_t it = 0;; it++) {
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w0) : "l"(w) : "memory");
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w1) : "l"(w + 1) : "memory");
-                if ((uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag) break;
-                if (it >= (1u << 22) || *(volatile int *)&fail_s) {
-                    ok = false;
-                    break;
-                }
-                __nanosleep(32);
-            }
-            sum += (int64_t)(((w1 & 0xffffffffull) << 32) | (w0 & 0xffffffffull));
-        }
-        if (!ok) {
-            fail_s = 1;
-            atomicCAS(a.error, 0, 5);
-            continue;
-        }
-        a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(sum));
+    const Step st = *a.step;
+    const uint32_t n = st.ar_base + a.ar_off;
+    const int H = a.ar.hidden;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= st.rows * H) return;
+    int64_t sum;
+    if (!ar_gather(a.ar, (int)(n & 1u), ar_tag(n), i / H, i % H, &fail_s, sum)) {
+        if (!fail_s) atomicCAS(a.error, 0, kErrArTimeout);
+        fail_s = 1;
+        sum = 0;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) *a.ar.epoch = epoch + 1;
+    a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(sum));
 }
 
 cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s) {
     ArFinishArgs c = a;
     void *args[] = {&c};
-    return launch_pdl((const void *)k_ar_finish, dim3(1), dim3(1024), args, s);
+    return launch_pdl((const void *)k_ar_finish, dim3((kMaxRows * a.ar.hidden + 255) / 256), dim3(256), args, s);
 }
 
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {

@@ -15,6 +15,8 @@ constexpr int kMaxRows = 8;   // kMaxTokensPerLaunch host:38
 struct Step {
     int32_t position;
     int32_t rows;
+    uint32_t ar_base;  // tensor parallel: number of the call's first all-reduce
+    int32_t pad;
 };
 
 enum Epi : int {
@@ -26,18 +28,37 @@ enum Epi : int {
 
 // Peer all-reduce over NVLink (tensor parallel): each rank owns one exchange
 // region and every rank stores its exact int64 partial sums straight into every
-// rank's region.  Each sum travels as two 64-bit words {32 data bits, 32-bit
-// tag = all-reduce number + 1}; a 64-bit store is single-copy atomic, so the
-// receiver polls the words themselves and needs no fence or flag.  Layout:
-//   256 B header | uint64 word[2 slots][kMaxTp sources][kMaxRows][hidden][2]
+// rank's region.  A sum travels as one 64-bit word {sum in the upper 48 bits,
+// 16-bit tag in the lower 16}; any partial sum of the path fits 48 bits
+// (|sum| < 2^15 * 2^15 * 11008 < 2^44).  A 64-bit store is single-copy atomic,
+// so the receiver polls the words themselves and needs no fence or flag.
+// All-reduce number n (counted per context, the same on every rank) uses slot
+// n & 1 and tag (n mod 65535) + 1.  Two slots suffice: a rank produces
+// all-reduce n + 2 only after every rank contributed to n + 1, which each rank
+// does only after its readers of n have finished.  Layout:
+//   256 B header | uint64 word[2 slots][kMaxTp sources][kMaxRows][hidden]
 constexpr int kMaxTp = 8;
 constexpr int kArHeader = 256;
+constexpr int kErrArTimeout = 5;  // device error code: a peer's sums did not arrive in time
 struct ArPeers {
     char *base[kMaxTp];  // exchange region of every rank (this rank's own included)
     int n;               // ranks (0: the partial sums stay local, NCCL reduces them)
     int me;
     int hidden;
-    int *epoch;          // this rank's count of finished all-reduces (slot = epoch & 1)
+    uint32_t poll_limit; // bounded wait for a peer's word (polls about 64 ns apart)
+};
+static __host__ __device__ __forceinline__ uint32_t ar_tag(uint32_t n) { return n % 65535u + 1u; }
+static __host__ __device__ __forceinline__ size_t ar_word_index(int slot, int src, int row, int hidden, int e) {
+    return (((size_t)slot * kMaxTp + src) * kMaxRows + row) * hidden + e;
+}
+// Consumer side of a peer all-reduce, fused into the next projection's
+// activation prologue: x = sat16(resid + round(sum over ranks)), also written
+// to hid_out by block 0 (the residual of the following sublayer).
+struct ArInput {
+    ArPeers ar;          // n <= 1: plain activation input
+    uint32_t ar_off;     // all-reduce number = step->ar_base + ar_off
+    const int16_t *resid;
+    int16_t *hid_out;
 };
 
 struct ProjArgs {
@@ -67,6 +88,8 @@ struct ProjArgs {
     int parts;           // warps sharing one unit along K (1, 2 or 4); G*B*parts consumer warps
     int *error;          // device word: nonzero after a bounded wait expired
     ArPeers ar;          // EPI_PARTIAL with ar.n > 1: push the sums to every rank
+    uint32_t ar_off;     // EPI_PARTIAL: all-reduce number = step->ar_base + ar_off
+    ArInput in;          // activation rows from a peer all-reduce (in.ar.n > 1) instead of x
     int row0;            // first row of this launch (x / out / resid already offset)
 };
 
@@ -122,6 +145,7 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
 
 struct ArFinishArgs {  // wait for every rank's sums, add them, round, + residual
     ArPeers ar;
+    uint32_t ar_off;
     const int16_t *resid;
     int16_t *out;
     const Step *step;
@@ -148,35 +172,6 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
 cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
                               const int32_t *row_of_slot, int nslots, uint32_t *dst,
                               cudaStream_t s);
-
-// Fused one-row decode of a whole layer stack (stack.cu): one persistent
-// cooperative kernel, phases separated by bounded grid barriers.
-struct StackArgs {
-    const uint32_t *wbuf;      // packed weights of all layers
-    size_t layer_words;        // words per layer
-    size_t off_o, off_gu, off_d; // word offsets of O, Gate/Up, Down within a layer
-    int H, Hq, KV, Il, hd, heads, gqa, max_seq;
-    int layer_begin, layer_count, final_norm;
-    const int16_t *norms, *rope, *etab, *ptab;
-    int16_t *kc, *vc;          // layer-0 caches; one layer = kv_heads*max_seq*hd further
-    int16_t *hid0, *hid1, *q, *att, *act;
-    int16_t *sc;               // [heads][max_seq] attention scores
-    int32_t *tmax;             // [heads][kStackMaxTiles] tile maxima
-    unsigned *bar;             // grid barrier counter, zero at launch
-    int *error;
-    const Step *step;
-    int32_t inv_elems, inv_rms_const, qk_scale;
-    int b_qkv, b_o, b_gu, b_d; // max units per ring chunk, per phase
-    int p_d;                   // warps sharing one Down unit (1, 2 or 4)
-    int x_bytes;               // activation / attention scratch bytes in shared memory
-    const int16_t *norm_final; // Task 20 norm row
-};
-constexpr int kStackMaxTiles = 40;  // max_seq <= 2560
-// Plan the fused kernel for a shape; false when the shape does not fit it.
-bool stack_plan(int H, int Hq, int KV, int Il, int hd, int max_seq, int nsm, StackArgs &a, size_t &smem);
-cudaError_t stack_configure(size_t smem);
-cudaError_t launch_stack(const StackArgs &a, size_t smem, int grid, cudaStream_t s);
-int stack_threads();
 
 // Greedy generation on the device (lm_head.cu, kernels.cu).  LM-head argmax
 // over caller-owned scratch of lm_argmax_scratch_bytes(); token-embedding

@@ -45,11 +45,11 @@ int fail_cuda(cudaError_t e, const char *what) {
         }                                                                     \
     } while (0)
 
-__global__ void k_set_step(Step *dst, int32_t position, int32_t rows, unsigned *bar) {
+__global__ void k_set_step(Step *dst, int32_t position, int32_t rows, uint32_t ar_base) {
     asm volatile("griddepcontrol.launch_dependents;");
     dst->position = position;
     dst->rows = rows;
-    if (bar) *bar = 0u;  // grid barrier counter of the fused decode kernel
+    dst->ar_base = ar_base;
 }
 
 int rows_template(uint32_t rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8; }
@@ -90,17 +90,14 @@ struct llmx_ctx {
     // slower); no gain at 8 rows.
     int attn_pf_tile_kb = 3584, attn_pf_kb = 72 * 1024, attn_pf_rows = 2;
     int attn_pf_late = 1;  // after attention's K/V loads (LLMX_ATTN_PREFETCH_LATE=0: at kernel start)
-    // fused one-row decode (stack.cu): plan, scratch, barrier counter
-    bool fused = false;
-    StackArgs stack{};
-    size_t stack_smem = 0;
-    int16_t *sc = nullptr;
-    int32_t *tmax = nullptr;
-    unsigned *bar = nullptr;
     // peer all-reduce (tensor parallel): exchange regions of every rank (IPC-mapped)
     ArPeers ar{};
     char *ar_region = nullptr;
     std::vector<char *> ar_opened;
+    // all-reduces enqueued so far (the same count on every rank); a call's first
+    // all-reduce number reaches the kernels in the step record
+    uint32_t ar_count = 0;
+    char *probe_region = nullptr;  // llmx_selftest_ar_timeout: an exchange region nobody writes
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -167,9 +164,11 @@ int env_int(const char *name, int def, int lo, int hi) {
     return x < lo ? lo : (x > hi ? hi : x);
 }
 
-int allreduce_resid(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
+// All-reduce `ar_off` of the call as a kernel of its own: wait for every rank's
+// sums, add, round, + residual (peer path); or NCCL + the rounding kernel.
+int allreduce_resid(llmx_ctx *c, uint32_t rows, uint32_t ar_off, int16_t *out, const int16_t *resid) {
     if (c->ar.n > 1) {  // the projection pushed its sums to every rank: wait, add, round
-        ArFinishArgs f{c->ar, resid, out, c->step, c->err};
+        ArFinishArgs f{c->ar, ar_off, resid, out, c->step, c->err};
         CK(launch_ar_finish(f, c->stream));
         c->launches += 1;
         return LLMX_OK;
@@ -286,9 +285,46 @@ ProjArgs down_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in)
     return d;
 }
 
-// Enqueue the kernels of one coarse task on the context stream.
+// A peer all-reduce whose finishing step is still to come: its number within
+// the call, the residual to add and where the finished rows belong.
+struct PendingAr {
+    bool active = false;
+    uint32_t off = 0;
+    const int16_t *resid = nullptr;
+    int16_t *out = nullptr;
+};
+
+// Route a projection's activation input through a pending peer all-reduce
+// (the projection's prologue finishes it).
+void take_input(llmx_ctx *c, ProjArgs &a, PendingAr &pend) {
+    if (!pend.active) return;
+    a.in.ar = c->ar;
+    a.in.ar_off = pend.off;
+    a.in.resid = pend.resid;
+    a.in.hid_out = pend.out;
+    pend.active = false;
+}
+
+// After a tensor-parallel O / Down projection: leave the all-reduce pending for
+// the next projection (peer path inside a stack) or finish it now.
+int after_partial(llmx_ctx *c, uint32_t rows, uint32_t &ar_next, int16_t *out, const int16_t *resid, bool fuse,
+                  PendingAr &pend) {
+    const uint32_t off = ar_next++;
+    if (fuse && c->ar.n > 1) {
+        pend.active = true;
+        pend.off = off;
+        pend.resid = resid;
+        pend.out = out;
+        return LLMX_OK;
+    }
+    return allreduce_resid(c, rows, off, out, resid);
+}
+
+// Enqueue the kernels of one coarse task on the context stream.  ar_next counts
+// the call's all-reduces; with `fuse` (stacks) the finishing step of a peer
+// all-reduce moves into the next projection's prologue (pend).
 int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32_t in_pair,
-                 uint32_t out_pair) {
+                 uint32_t out_pair, uint32_t &ar_next, bool fuse, PendingAr &pend) {
     const llmx_shape &s = c->s;
     const int rt = rows_template(rows);
     const int16_t *in = c->hid[in_pair];
@@ -296,6 +332,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         ProjArgs a = qkv_args(c, layer, in);
+        take_input(c, a, pend);
         set_stages(c, a, EPI_QKV, rt);
         CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         AttnArgs t = attn_args(c, layer);
@@ -303,17 +340,20 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
         CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
+        o.ar_off = ar_next;
         set_stages(c, o, ge, rt);
         CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
         c->launches += 3;
-        if (c->size > 1) return allreduce_resid(c, rows, out, in);
+        if (c->size > 1) return after_partial(c, rows, ar_next, out, in, fuse, pend);
         return LLMX_OK;
     }
     if (op == LLMX_OP_FFN_SUBLAYER) {
         ProjArgs g = gu_args(c, layer, in);
+        take_input(c, g, pend);
         set_stages(c, g, EPI_SILU, rt);
         CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
         ProjArgs d = down_args(c, layer, out, in);
+        d.ar_off = ar_next;
         if (rt == 8 && c->size == 1) {
             // an 8-row block as two 4-row launches: 8 FFN-wide activation rows would
             // fill shared memory and starve the weight ring; 4 rows leave it room
@@ -332,7 +372,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
             CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
             c->launches += 2;
         }
-        if (c->size > 1) return allreduce_resid(c, rows, out, in);
+        if (c->size > 1) return after_partial(c, rows, ar_next, out, in, fuse, pend);
         return LLMX_OK;
     }
     if (op == LLMX_OP_FINAL_NORM) {
@@ -345,8 +385,14 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     return LLMX_OK;  // NOP
 }
 
+// All-reduces of one coarse task / one stack (tensor parallel).
+uint32_t task_allreduces(const llmx_ctx *c, uint32_t op) {
+    return c->size > 1 && (op == LLMX_OP_ATTENTION_SUBLAYER || op == LLMX_OP_FFN_SUBLAYER) ? 1u : 0u;
+}
+uint32_t stack_allreduces(const llmx_ctx *c, uint32_t layer_count) { return c->size > 1 ? 2u * layer_count : 0u; }
+
 int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
-    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows, c->bar);
+    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows, c->ar_count);
     CK(cudaGetLastError());
     c->launches += 1;
     return LLMX_OK;
@@ -376,14 +422,23 @@ bool model_ready(const llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count) 
 }
 
 // Kernels of a stack, enqueued (graph capture body).
+// On the peer all-reduce path each all-reduce is finished by the next
+// projection's prologue (Gate/Up after O, the next layer's QKV after Down); only
+// the stack's last one runs as a kernel of its own.
 int enqueue_stack(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, int final_norm) {
+    uint32_t ar_next = 0;
+    PendingAr pend;
     for (uint32_t l = layer_begin; l < layer_begin + layer_count; l++) {
-        int rc = enqueue_task(c, LLMX_OP_ATTENTION_SUBLAYER, l, rows, 1, 0);
+        int rc = enqueue_task(c, LLMX_OP_ATTENTION_SUBLAYER, l, rows, 1, 0, ar_next, true, pend);
         if (rc) return rc;
-        rc = enqueue_task(c, LLMX_OP_FFN_SUBLAYER, l, rows, 0, 1);
+        rc = enqueue_task(c, LLMX_OP_FFN_SUBLAYER, l, rows, 0, 1, ar_next, true, pend);
         if (rc) return rc;
     }
-    if (final_norm) return enqueue_task(c, LLMX_OP_FINAL_NORM, 0, rows, 1, 0);
+    if (pend.active) {
+        const int rc = allreduce_resid(c, rows, pend.off, pend.out, pend.resid);
+        if (rc) return rc;
+    }
+    if (final_norm) return enqueue_task(c, LLMX_OP_FINAL_NORM, 0, rows, 1, 0, ar_next, false, pend);
     return LLMX_OK;
 }
 
@@ -410,73 +465,70 @@ int launch_stack_graph(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_
     }
     CK(cudaGraphLaunch(it->second.first, c->stream));
     c->launches += it->second.second;
+    c->ar_count += stack_allreduces(c, layer_count);
     return LLMX_OK;
 }
 
-// One-row stacks on one GPU run as a single cooperative kernel (stack.cu).
-bool use_fused(const llmx_ctx *c, uint32_t rows) { return c->fused && rows == 1; }
-
-int launch_fused(llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count, int final_norm) {
-    StackArgs a = c->stack;
-    a.layer_begin = (int)layer_begin;
-    a.layer_count = (int)layer_count;
-    a.final_norm = final_norm;
-    CK(launch_stack(a, c->stack_smem, c->nsm, c->stream));
-    c->launches += 1;
-    return LLMX_OK;
-}
-
-// Step record + the stack (fused kernel for one row when enabled, else the
-// captured graph).  Arguments already validated.
+// Step record + the stack (its captured graph).  Arguments already validated.
 int launch_stack_at(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, uint32_t position,
                     int final_norm) {
     int rc = set_step(c, position, rows);
     if (rc) return rc;
-    if (use_fused(c, rows)) return launch_fused(c, layer_begin, layer_count, final_norm);
     return launch_stack_graph(c, rows, layer_begin, layer_count, final_norm);
 }
 
 // Peer all-reduce set-up: one zeroed exchange region per rank, its IPC handle
-// all-gathered over NCCL, the other ranks' regions mapped.  If a peer region
-// cannot be mapped the context keeps the NCCL all-reduce.
-int setup_peer_allreduce(llmx_ctx *c) {
-    const size_t bytes = kArHeader + (size_t)2 * kMaxTp * kMaxRows * c->s.hidden * 2 * sizeof(uint64_t);
+// all-gathered over NCCL, the other ranks' regions mapped.  Every rank must take
+// the same path (a rank on NCCL and one on peer stores would wait on each other
+// for good), so the ranks agree over NCCL: the peer path is used only if every
+// rank wants it (LLMX_TP_NCCL unset) and mapped every peer region; otherwise
+// every rank unmaps what it opened and keeps the NCCL all-reduce.
+int setup_peer_allreduce(llmx_ctx *c, bool want_peer) {
+    const size_t bytes = kArHeader + (size_t)2 * kMaxTp * kMaxRows * c->s.hidden * sizeof(uint64_t);
     int rc;
-    int *epoch = nullptr;
     char *hbuf = nullptr;
-    if ((rc = dalloc(c, &c->ar_region, bytes)) || (rc = dalloc(c, &epoch, 1)) ||
-        (rc = dalloc(c, &hbuf, (size_t)c->size * sizeof(cudaIpcMemHandle_t))))
+    int *okbuf = nullptr;
+    if ((rc = dalloc(c, &hbuf, (size_t)c->size * sizeof(cudaIpcMemHandle_t))) || (rc = dalloc(c, &okbuf, 1)))
         return rc;
-    CK(cudaMemset(c->ar_region, 0, bytes));
-    CK(cudaMemset(epoch, 0, sizeof(int)));
-    cudaIpcMemHandle_t mine;
-    CK(cudaIpcGetMemHandle(&mine, c->ar_region));
+    cudaIpcMemHandle_t mine{};
+    int ok = want_peer && c->size <= kMaxTp ? 1 : 0;
+    if (ok) {
+        if ((rc = dalloc(c, &c->ar_region, bytes))) return rc;
+        CK(cudaIpcGetMemHandle(&mine, c->ar_region));
+    }
     CK(cudaMemcpy(hbuf + (size_t)c->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice));
     CKN(ncclAllGather(hbuf + (size_t)c->rank * sizeof(mine), hbuf, sizeof(mine), ncclChar, c->comm, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     std::vector<cudaIpcMemHandle_t> all(c->size);
     CK(cudaMemcpy(all.data(), hbuf, all.size() * sizeof(mine), cudaMemcpyDeviceToHost));
     ArPeers a{};
-    for (int p = 0; p < c->size; p++) {
+    for (int p = 0; p < c->size && ok; p++) {
         if (p == c->rank) {
             a.base[p] = c->ar_region;
             continue;
         }
         void *ptr = nullptr;
-        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            for (char *q : c->ar_opened) cudaIpcCloseMemHandle(q);
-            c->ar_opened.clear();
-            return LLMX_OK;  // keep the NCCL all-reduce
+        if (cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            (void)cudaGetLastError();
+            ok = 0;
+            break;
         }
         a.base[p] = static_cast<char *>(ptr);
         c->ar_opened.push_back(a.base[p]);
     }
+    CK(cudaMemcpy(okbuf, &ok, sizeof(int), cudaMemcpyHostToDevice));
+    CKN(ncclAllReduce(okbuf, okbuf, 1, ncclInt32, ncclMin, c->comm, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(&ok, okbuf, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!ok) {
+        for (char *q : c->ar_opened) cudaIpcCloseMemHandle(q);
+        c->ar_opened.clear();
+        return LLMX_OK;  // every rank keeps the NCCL all-reduce
+    }
     a.n = c->size;
     a.me = c->rank;
     a.hidden = c->s.hidden;
-    a.epoch = epoch;
+    a.poll_limit = (uint32_t)env_int("LLMX_AR_POLL_LIMIT", 1 << 24, 1, 1 << 30);
     c->ar = a;
     return LLMX_OK;
 }
@@ -634,57 +686,6 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         c->inv_rms_const = inv_rms_q88(0, 0);
         c->qk_scale = qk_scale_q1616(hd);
     }
-    // fused one-row decode (opt-in, LLMX_FUSED_DECODE=1): one GPU, a shape the
-    // kernel's plan accepts, and a cooperative launch of one CTA per SM
-    if (tp_size == 1 && env_int("LLMX_FUSED_DECODE", 0, 0, 1) == 1) {
-        StackArgs &a = c->stack;
-        size_t smem = 0;
-        int coop = 0;
-        e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-        if (e != cudaSuccess) return bail(fail_cuda(e, "cudaDeviceGetAttribute"));
-        if (coop && stack_plan(s.hidden, c->Hq, c->KV, c->Il, hd, s.max_seq, c->nsm, a, smem) &&
-            stack_configure(smem) == cudaSuccess) {
-            if ((rc = dalloc(c, &c->sc, (size_t)s.heads * s.max_seq)) ||
-                (rc = dalloc(c, &c->tmax, (size_t)s.heads * kStackMaxTiles)) || (rc = dalloc(c, &c->bar, 1)))
-                return bail(rc);
-            a.wbuf = c->wbuf;
-            a.layer_words = c->layer_words;
-            a.off_o = c->w_qkv;
-            a.off_gu = c->w_qkv + c->w_o;
-            a.off_d = c->w_qkv + c->w_o + c->w_gu;
-            a.H = s.hidden;
-            a.Hq = c->Hq;
-            a.KV = c->KV;
-            a.Il = c->Il;
-            a.hd = hd;
-            a.heads = s.heads;
-            a.gqa = G;
-            a.max_seq = s.max_seq;
-            a.norms = c->norms;
-            a.norm_final = c->norms + (size_t)2 * s.layers * s.hidden;
-            a.rope = c->rope;
-            a.etab = c->etab;
-            a.ptab = c->ptab;
-            a.kc = c->kc;
-            a.vc = c->vc;
-            a.hid0 = c->hid[0];
-            a.hid1 = c->hid[1];
-            a.q = c->q;
-            a.att = c->att;
-            a.act = c->act;
-            a.sc = c->sc;
-            a.tmax = c->tmax;
-            a.bar = c->bar;
-            a.error = c->err;
-            a.step = c->step;
-            a.inv_elems = c->inv_elems;
-            a.inv_rms_const = c->inv_rms_const;
-            a.qk_scale = c->qk_scale;
-            c->stack_smem = smem;
-            c->fused = true;
-        }
-        cudaGetLastError();  // a refused smem opt-in only disables the fused path
-    }
     if (tp_size > 1) {
         ncclUniqueId id;
         std::memcpy(&id, tp_id, sizeof(id));
@@ -693,8 +694,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
             g_last_error = std::string("ncclCommInitRank: ") + ncclGetErrorString(r);
             return bail(LLMX_ERR_NCCL);
         }
-        if (tp_size <= kMaxTp && env_int("LLMX_TP_NCCL", 0, 0, 1) == 0 && (rc = setup_peer_allreduce(c)))
-            return bail(rc);
+        if ((rc = setup_peer_allreduce(c, env_int("LLMX_TP_NCCL", 0, 0, 1) == 0))) return bail(rc);
     }
     *out = c;
     return LLMX_OK;
@@ -823,8 +823,11 @@ int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint3
     CK(cudaSetDevice(c->dev));
     const uint64_t before = c->launches;
     int rc = set_step(c, position, rows);
-    if (!rc) rc = enqueue_task(c, op, layer, rows, c->in_pair, c->out_pair);
+    uint32_t ar_next = 0;
+    PendingAr pend;
+    if (!rc) rc = enqueue_task(c, op, layer, rows, c->in_pair, c->out_pair, ar_next, false, pend);
     if (rc) return rc;
+    c->ar_count += task_allreduces(c, op);
     CK(cudaStreamSynchronize(c->stream));
     c->last_launches = c->launches - before;
     return check_device_error(c);
@@ -950,6 +953,31 @@ void *llmx_stream(llmx_ctx *c) { return c ? (void *)c->stream : nullptr; }
 void *llmx_hidden_device_ptr(llmx_ctx *c, uint32_t pair) { return c && pair < 2 ? c->hid[pair] : nullptr; }
 uint64_t llmx_kernel_launches(const llmx_ctx *c) { return c ? c->last_launches : 0; }
 uint64_t llmx_device_bytes(const llmx_ctx *c) { return c ? c->device_bytes : 0; }
+
+int llmx_selftest_ar_timeout(llmx_ctx *c, uint32_t poll_limit) {
+    if (!c || poll_limit == 0) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    const size_t bytes = kArHeader + (size_t)2 * kMaxTp * kMaxRows * c->s.hidden * sizeof(uint64_t);
+    int rc;
+    if (!c->probe_region && (rc = dalloc(c, &c->probe_region, bytes))) return rc;
+    ArPeers a{};
+    a.base[0] = c->probe_region;  // zeroed words: no tag ever matches
+    a.n = 1;
+    a.me = 0;
+    a.hidden = c->s.hidden;
+    a.poll_limit = poll_limit;
+    if ((rc = set_step(c, 0, 1))) return rc;
+    ArFinishArgs f{a, 0, c->hid[1], c->hid[0], c->step, c->err};
+    CK(launch_ar_finish(f, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
+}
+
+int llmx_allreduce_kind(const llmx_ctx *c) {
+    if (!c) return -1;
+    if (c->size == 1) return LLMX_AR_NONE;
+    return c->ar.n > 1 ? LLMX_AR_PEER : LLMX_AR_NCCL;
+}
 
 int llmx_run_prompt_block(llmx_ctx *c, const llmx_model *m, const uint32_t *tokens, uint32_t n, uint32_t position,
                           int materialize, int16_t *hidden_out) {

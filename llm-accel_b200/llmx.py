@@ -25,6 +25,7 @@ OK = 0
 BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 3, 4, 5
 ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED, ERR_TIMEOUT = range(100, 109)
 OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
+AR_NONE, AR_NCCL, AR_PEER = 0, 1, 2
 MAX_ROWS = 8
 KERNEL_QKV, KERNEL_ATTN, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(6)
 
@@ -123,6 +124,8 @@ def lib():
             "llmx_run_token": (C.c_int, [vp, vp, C.c_uint32, C.c_uint32, i16p]),
             "llmx_lm_head_argmax_device": (C.c_int, [vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp]),
             "llmx_upload_vocab": (C.c_int, [vp, vp]),
+            "llmx_allreduce_kind": (C.c_int, [vp]),
+            "llmx_selftest_ar_timeout": (C.c_int, [vp, C.c_uint32]),
             "llmx_generate": (C.c_int, [vp, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp]),
         }
         for name, (res, args) in sig.items():
@@ -369,6 +372,15 @@ class Accelerator:
     @property
     def device_bytes(self):
         return lib().llmx_device_bytes(self.h)
+
+    def selftest_ar_timeout(self, poll_limit):
+        """Return code of a bounded all-reduce wait that is made to expire (LLMX_ERR_TIMEOUT)."""
+        return lib().llmx_selftest_ar_timeout(self.h, poll_limit)
+
+    @property
+    def allreduce_kind(self):
+        """AR_NONE (one GPU), AR_NCCL or AR_PEER: how the ranks add their partial sums."""
+        return lib().llmx_allreduce_kind(self.h)
 
     def upload_vocab(self, m: Model):
         check(lib().llmx_upload_vocab(self.h, m.h), "upload_vocab")

@@ -189,3 +189,19 @@ def test_status_and_errors_on_device(llmx, small):
     assert acc.task(llmx.OP_ATTENTION, 0, s.max_seq - 2, 3, raise_on_error=False)[0] == llmx.BAD_POSITION
     rc, st = acc.task(llmx.OP_NOP, 0, 0, 1, raise_on_error=False)
     assert rc == 0 and st.op == 0 and st.last_task == 1
+
+
+def test_bounded_wait_expires_with_error_status(llmx, oracle, small):
+    """Failure detection without a fault: the receiving side of the peer
+    all-reduce waits on an exchange region that nothing writes; the bounded
+    wait expires, the kernel records its error status and returns, the call
+    reports LLMX_ERR_TIMEOUT, and the same context then runs a stack that
+    matches the oracle."""
+    s, m, acc, layers = small
+    assert acc.selftest_ar_timeout(2000) == llmx.ERR_TIMEOUT
+    assert "bounded wait expired" in llmx.last_error()
+    assert acc.selftest_ar_timeout(0) == llmx.ERR_ARG
+    acc.reset_kv()
+    ref = OracleState(oracle, oracle_shape(oracle, s), layers, m.norms())
+    h = np.random.default_rng(9).integers(-600, 600, (3, s.hidden)).astype(np.int16)
+    _assert_same(acc.stack(h, position=0), ref.stack(h, 0), "stack after the expired wait")

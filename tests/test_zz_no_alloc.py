@@ -49,6 +49,18 @@ def test_lm_head_argmax_device_matches_host(llmx):
     assert t8.cpu().numpy().astype(np.uint32).tolist() == want8
     assert want8[3] == 0
 
+    # the one- / two-vocabulary-row-per-warp variants (rows 2 and 3 -> 4) on
+    # row subsets; after the first call's set-up no call allocates device memory
+    for n in (2, 3):
+        tn = torch.zeros(n, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info(dev)[0]
+        rc = llmx.lm_head_argmax_device(d8.data_ptr(), n, s.hidden, w.data_ptr(), s.vocab, tn.data_ptr(), stream)
+        assert rc == llmx.OK, llmx.last_error()
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info(dev)[0] == free1, "the call allocated device memory"
+        assert tn.cpu().numpy().astype(np.uint32).tolist() == want8[:n]
+
     # more rows than the scratch holds: rejected before any launch
     rc = llmx.lm_head_argmax_device(d8.data_ptr(), 9, s.hidden, w.data_ptr(), s.vocab, t8.data_ptr(), stream)
     assert rc == llmx.ERR_ARG and "rows must be 1..8" in llmx.last_error()
