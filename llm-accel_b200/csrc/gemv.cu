@@ -73,17 +73,16 @@ static __device__ void stage_rows_allreduce(const ProjArgs &a, const Step &st, i
     consumer_sync();
 }
 
-// In-place RMSNorm of rows already staged in shared memory (all-reduce input).
+// In-place RMSNorm of rows already staged in shared memory (all-reduce input);
+// red / inv_rms_s: the staging prologue's reduction scratch.
 template <int R>
-static __device__ void norm_rows_smem(const ProjArgs &a, int16_t *xs, int rows, int tid) {
-    constexpr int CW = Warps<R>::kConsumers;
+static __device__ void norm_rows_smem(const ProjArgs &a, int16_t *xs, int rows, int tid,
+                                      int64_t (*red)[kMaxRows], int32_t *inv_rms_s) {
     const int T = blockDim.x - 32, cw = T / 32;
     const int K = a.K, KV8 = K >> 3;
-    __shared__ int32_t inv_rms_s[kMaxRows];
     if (a.inv_elems == 0) {
         if (tid < R) inv_rms_s[tid] = a.inv_rms_const;
     } else {
-        __shared__ int64_t red[CW][kMaxRows];
         int64_t part[R];
 #pragma unroll
         for (int r = 0; r < R; r++) part[r] = 0;
@@ -134,18 +133,18 @@ static __device__ void stage_rows(const ProjArgs &a, const Step &st, int16_t *xs
     constexpr int CW = Warps<R>::kConsumers;  // upper bound of the consumer warps
     const int T = blockDim.x - 32, cw = T / 32;
     const int K = a.K, KV8 = K >> 3;
+    __shared__ int32_t inv_rms_s[kMaxRows];
+    __shared__ int64_t red[CW][kMaxRows];
     if (a.in.ar.n > 1) {  // tensor parallel: the previous projection's all-reduce, finished here
         stage_rows_allreduce<R>(a, st, xs, rows, tid);
-        if (a.norm != nullptr) norm_rows_smem<R>(a, xs, rows, tid);
+        if (a.norm != nullptr) norm_rows_smem<R>(a, xs, rows, tid, red, inv_rms_s);
         return;
     }
-    __shared__ int32_t inv_rms_s[kMaxRows];
     if (a.norm != nullptr) {
         if (a.inv_elems == 0) {
             // recip(fm(K)) == 0: mean == 0 for every input, inv_rms is a constant
             if (tid < R) inv_rms_s[tid] = a.inv_rms_const;
         } else {
-            __shared__ int64_t red[CW][kMaxRows];
             int64_t part[R];
 #pragma unroll
             for (int r = 0; r < R; r++) part[r] = 0;
