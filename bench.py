@@ -41,6 +41,14 @@ CONFIGS = {
 }
 
 
+def bench_config(cfg_id, world, P, K):
+    """The `config` object of both arms (same keys)."""
+    return {"workload": CONFIGS[cfg_id]["name"], "layers": 36, "hidden": 2048, "ffn": 11008, "heads": 16,
+            "kv_heads": 2, "prompt_tokens": P, "decode_positions": [P, P + K - 1], "rows_per_decode": 1,
+            "sequence_batch": 1, "parallelism": f"tp{world}",
+            "l2": "no flush: every step streams 5.5 GB/N of weights (>> 126 MB L2)"}
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -261,8 +269,18 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
         gen = generate_leg(acc, model, shape, prompt, device_time, stream)
 
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(acc, model, shape, rows[P:], P, e2e_outputs)
+    if not args.no_cpu_baseline:
+        # parity of this run: the device's post-prefill KV of layers 0-1 against
+        # the oracle's own prefill of those layers; decode rows against the oracle
+        # (N=1: a timed sample; N>1: one forward on rank 0, and every rank's row)
+        kv_ok = prefill_kv_check(acc, shape, rows[:P], P, rank) if rank == 0 else None
+        if world == 1:
+            cpu = cpu_baseline(acc, model, shape, rows[P:], P, e2e_outputs)
+        else:
+            cpu = tp_parity(acc, shape, rank, world, dist, rows[P:], P, e2e_outputs[0])
+        if rank == 0:
+            cpu["prefill_kv_layers_0_1_match"] = kv_ok
+            cpu["matches_gpu"] = bool(cpu["matches_gpu"] and kv_ok)
 
     result = {
         "metric": METRIC,
@@ -278,20 +296,18 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
         "dtype": "int16",
         "data": "synthetic: seeded N(0,0.02)->Q4.12 weights, N(0,1)->Q8.8 embedding rows, norm weights 1.0 "
                 "(random-init, no checkpoint)",
-        "config": {"workload": cfg["name"], "layers": L, "hidden": H, "ffn": shape.inter, "heads": shape.heads,
-                   "kv_heads": shape.kv_heads, "prompt_tokens": P,
-                   "decode_positions": [P, P + K - 1], "rows_per_decode": 1, "sequence_batch": 1,
-                   "parallelism": f"tp{world}",
-                   "l2": "no flush: every step streams 5.5 GB/N of weights (>> 126 MB L2)"},
+        "config": bench_config(cfg_id, world, P, K),
         "prefill": {"value": P / (prefill_ms * 1e-3), "unit": "tok/s", "ms_per_p8_block": prefill_ms / (P // 8),
                     "hbm_frac": (P // 8) * bytes_per_decode(shape, world, P // 2) / (prefill_ms * 1e-3) / 1e9
                     / peak},
         "decode_roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peak, "unit": "GB/s",
                             "frac": dec_gbs / peak, "bytes_per_step": int(np.mean(step_bytes)),
                             "peak_source": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": "k_proj<1,EPI_SILU> (RMSNorm + Gate/Up + SiLU x Up, decode)",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv<1,EPI_SILU,8,1> (RMSNorm + Gate/Up + SiLU x Up, decode)",
                      "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-                     "traffic": ncu_traffic("gate_up_decode_ncu.txt"), "bytes_per_launch": gu_bytes,
+                     # ncu dram bytes only from a capture of this same launch shape (one GPU, full FFN)
+                     "traffic": ncu_traffic("gate_up_decode_ncu.txt") if world == 1 else None,
+                     "bytes_per_launch": gu_bytes,
                      "ms_per_launch": gu_ms, "down_ms_per_launch": down_ms, "peak_source": peak_kind},
         "e2e": {"value": K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
                 "d2h_bytes_per_step": H * 2, "wall_ms_per_step": e2e_wall_ms / K,
@@ -355,6 +371,70 @@ def generate_leg(acc, model, shape, prompt, device_time, stream, new_tokens=64):
             "lm_head_argmax_ms": am_ms, "lm_head_gbs": shape.vocab * shape.hidden * 2 / (am_ms * 1e-3) / 1e9,
             "host_lm_head_argmax_ms": host_ms, "host_threads": os.cpu_count(), "vocab_upload_s": upload_s,
             "api": "llmx_generate (device embedding gather + stack + LM-head argmax, one host wait)"}
+
+
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle as O
+    O.set_exp_mode(O.EXP_TRUNC)
+    return O
+
+
+def _dense_layers(O, shape, layers):
+    s = O.shape("qwen2.5-3b", max_seq=shape.max_seq)
+    return s, [O.gaussian_layer(s, SEED, l, W_SIGMA) for l in layers]
+
+
+def prefill_kv_check(acc, shape, prompt_rows, P, rank):
+    """The oracle's own prefill of layers 0 and 1 (P/8 P8 blocks, all host
+    threads) against the device's K/V cache of those layers after the prompt."""
+    O = _oracle()
+    from helpers import OracleState
+    O.set_threads(len(os.sched_getaffinity(0)))
+    s, dense = _dense_layers(O, shape, [0, 1])
+    norms = np.full((2 * shape.layers + 1, s.hidden), 256, np.int16)
+    s2 = O.shape("qwen2.5-3b", max_seq=shape.max_seq, layers=2)
+    ref = OracleState(O, s2, dense, norms[:5])
+    ok = True
+    for b in range(P // 8):
+        ref.stack(prompt_rows[8 * b:8 * b + 8], 8 * b, final_norm=False)
+    for l in range(2):
+        k, v = acc.read_kv(l, 0, P)
+        ok &= bool(np.array_equal(k, ref.kc[l][:, :P]) and np.array_equal(v, ref.vc[l][:, :P]))
+    O.set_threads(1)
+    return ok
+
+
+def tp_parity(acc, shape, rank, world, dist, dec_rows, P, first_out):
+    """Tensor parallel: every rank's first end-to-end decode row must be the same,
+    and rank 0 recomputes it with the oracle (1 thread, all 36 layers, from the
+    device KV of positions < P, which every rank holds in full)."""
+    import torch
+    mine = torch.from_numpy(np.ascontiguousarray(first_out, np.int16)).cuda()
+    allo = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allo, mine)
+    same = all(torch.equal(allo[0], t) for t in allo)
+    res = None
+    if rank == 0:
+        O = _oracle()
+        from helpers import OracleState
+        s, dense = _dense_layers(O, shape, range(shape.layers))
+        norms = np.full((2 * shape.layers + 1, s.hidden), 256, np.int16)
+        ref = OracleState(O, s, dense, norms)
+        for l in range(shape.layers):
+            k, v = acc.read_kv(l, 0, P)
+            ref.kc[l][:, :P] = k
+            ref.vc[l][:, :P] = v
+        t0 = time.time()
+        out = ref.stack(dec_rows[0:1], P)
+        dt = time.time() - t0
+        res = {"value": 1.0 / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"1 decode forward (36 layers + final norm) at position {P} from the device KV state, "
+                         f"integer oracle restatement, 1 thread",
+               "matches_gpu": bool(same and np.array_equal(out, first_out)), "ranks_identical": bool(same)}
+    dist.barrier()
+    return res
 
 
 def cpu_baseline(acc, model, shape, dec_rows, P, gpu_outputs):
@@ -427,7 +507,7 @@ def run_reference(args, cfg_id, world, K, W):
         "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": dt * 1e3 / K, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int16", "data": "synthetic (same seeds as the llmx arm)",
-        "config": {"workload": CONFIGS[cfg_id]["name"], "prompt_tokens": P, "decode_positions": [P, P + K - 1]},
+        "config": bench_config(cfg_id, world, P, K),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
                          "sample": f"{K} decode forwards (36 layers + final norm) at positions {P}..{P + K - 1}, "
                                    f"oracle restatement of the reference golden model, {cores} threads"},

@@ -308,6 +308,11 @@ def gaussian_layer(s: Shape, seed: int, layer: int, w_sigma: float = 0.02):
                            for op, n in enumerate(sizes)])
 
 
+def gaussian_lm_head(s: Shape, seed: int, w_sigma: float = 0.02):
+    """Untied LM head of the synthetic model: N(0, w_sigma) in Q4.12, stream 0x20."""
+    return gauss_fill(seed, 0x20, w_sigma * 4096.0, s.vocab * s.hidden).reshape(s.vocab, s.hidden)
+
+
 def gaussian_embedding_rows(s: Shape, seed: int, tokens):
     """Embedding rows of the synthetic model: N(0, 1) in Q8.8, stream 0x10."""
     return np.stack([gauss_fill(seed, 0x10, 256.0, s.hidden, int(t) * s.hidden) for t in tokens])

@@ -64,9 +64,10 @@ def test_small_generate_matches_host_loop_and_oracle(llmx, oracle, block_rows):
     acc.close()
 
 
-def test_generate_gaussian_untied_and_layer_count(llmx):
+def test_generate_gaussian_untied_and_layer_count(llmx, oracle):
     """Synthetic Gaussian model with an untied LM head; only the first two of
-    three layers run (layer_count)."""
+    three layers run (layer_count).  The device loop must equal the host loop
+    and the oracle's incremental stack + argmax over the regenerated head."""
     s = llmx.shape("qwen2.5-3b", layers=3, max_seq=64, vocab=4096)
     m = llmx.Model(s).init_gaussian(20260718, 0.02, lm_head=True)
     acc = llmx.Accelerator(s)
@@ -87,6 +88,20 @@ def test_generate_gaussian_untied_and_layer_count(llmx):
         if step < 5:
             h = acc.stack(m.embed([want[-1]]), layer_count=2, position=len(prompt) + step)
     assert got == want
+    # oracle leg: its own prompt blocks + decodes over layers 0-1, argmax over the
+    # LM head regenerated from its seed (stream 0x20, N(0, 0.02) in Q4.12)
+    ref = OracleState(oracle, oracle_shape(oracle, s), [m.layer(0), m.layer(1)], m.norms())
+    head = oracle.gaussian_lm_head(oracle_shape(oracle, s), 20260718, 0.02)
+    for b0 in range(0, len(prompt), 8):
+        blk = prompt[b0:b0 + 8]
+        o = ref.stack(m.embed(blk), b0, layer_count=2, final_norm=b0 + len(blk) == len(prompt))
+    ref_tokens = []
+    for step in range(6):
+        ref_tokens.append(oracle.lm_head_argmax(o[-1], head))
+        if step < 5:
+            o = ref.stack(m.embed([ref_tokens[-1]]), len(prompt) + step, layer_count=2)
+    assert got == ref_tokens
+    assert m.lm_head_argmax(o[-1]) == oracle.lm_head_argmax(o[-1], head)
     acc.close()
 
 

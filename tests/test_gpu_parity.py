@@ -205,3 +205,32 @@ def test_bounded_wait_expires_with_error_status(llmx, oracle, small):
     ref = OracleState(oracle, oracle_shape(oracle, s), layers, m.norms())
     h = np.random.default_rng(9).integers(-600, 600, (3, s.hidden)).astype(np.int16)
     _assert_same(acc.stack(h, position=0), ref.stack(h, 0), "stack after the expired wait")
+
+
+def test_prefill_sweep_device_built_cache(llmx, oracle):
+    """BASELINE config 2 on one Qwen2.5-3B-shaped layer (Gaussian weights, N(0,1)
+    embedding rows): a 1024-token prompt as 128 consecutive P8 blocks, the KV
+    cache built by the device itself (nothing preloaded).  Prompts of 8, 64,
+    256 and 1024 tokens are its prefixes.  Every block's final-normed rows are
+    compared with the oracle's incremental state, and the whole K/V cache at
+    each prompt length (the reference's P/D sweep,
+    results/q214-pd-20260811/performance.tsv:2-9)."""
+    s = llmx.shape("qwen2.5-3b", layers=1, max_seq=1024, vocab=4096)
+    m = llmx.Model(s).init_gaussian(20260718, 0.02)
+    acc = llmx.Accelerator(s)
+    acc.upload_model(m)
+    oracle.set_threads(8)
+    ref = OracleState(oracle, oracle_shape(oracle, s), [m.layer(0)], m.norms())
+    toks = np.random.default_rng(1024).integers(0, s.vocab, 1024)
+    try:
+        for b in range(128):
+            h = m.embed(toks[8 * b:8 * b + 8])
+            _assert_same(acc.stack(h, position=8 * b), ref.stack(h, 8 * b), f"P8 block {b}")
+            n = 8 * (b + 1)
+            if n in (8, 64, 256, 1024):
+                k, v = acc.read_kv(0, 0, n)
+                _assert_same(k, ref.kc[0][:, :n], f"K cache after {n} prompt tokens")
+                _assert_same(v, ref.vc[0][:, :n], f"V cache after {n} prompt tokens")
+    finally:
+        oracle.set_threads(1)
+        acc.close()
