@@ -411,7 +411,7 @@ def tp_parity(acc, shape, rank, world, dist, dec_rows, P, first_out):
     and rank 0 recomputes it with the oracle (1 thread, all 36 layers, from the
     device KV of positions < P, which every rank holds in full)."""
     import torch
-    mine = torch.from_numpy(np.ascontiguousarray(first_out, np.int16)).cuda()
+    mine = torch.from_numpy(np.ascontiguousarray(first_out, np.int32)).cuda()  # NCCL has no int16
     allo = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(allo, mine)
     same = all(torch.equal(allo[0], t) for t in allo)
