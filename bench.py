@@ -256,6 +256,9 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
 
     # dominant kernel (Gate/Up + SiLU, ~59% of the decode bytes): mean device time per launch
     Il = shape.inter // world
+    # every kernel of a decode layer at context P + 1 on this rank (no all-reduce in these launches)
+    kernel_us = {n: acc.time_kernel(i, 0, P, 1, 2 * L) * 1e3
+                 for i, n in enumerate(["qkv", "attention", "o_proj", "gate_up", "down", "final_norm"])}
     gu_ms = acc.time_kernel(llmx.KERNEL_GATE_UP, 0, P, 1, 3 * L)
     down_ms = acc.time_kernel(llmx.KERNEL_DOWN, 0, P, 1, 3 * L)
     gu_bytes = 2 * Il * H * 2 + H * 2 + H * 2 + Il * 2
@@ -312,6 +315,7 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
         "e2e": {"value": K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
                 "d2h_bytes_per_step": H * 2, "wall_ms_per_step": e2e_wall_ms / K,
                 "api": "llmx_stack (run_token boundary: host embedding-table row -> H2D -> 36x Task18/19 -> Task20 -> D2H)"},
+        "kernel_us": kernel_us,
         "gpu_launches": gpu_launches,
         "clocks": clock,
         "setup_s": setup_s,

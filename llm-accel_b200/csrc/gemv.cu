@@ -55,20 +55,24 @@ static __device__ void stage_rows_allreduce(const ProjArgs &a, const Step &st, i
     __shared__ int fail_s;
     if (tid == 0) fail_s = 0;
     consumer_sync();
-    for (int i = tid; i < R * K; i += T) {
+    for (int i = 4 * tid; i < R * K; i += 4 * T) {  // 4 consecutive elements per step (K % 8 == 0)
         const int r = i / K, e = i - r * K;
-        int16_t x = 0;
+        uint2 x = make_uint2(0, 0);
         if (r < rows) {
-            int64_t sum;
-            if (!ar_gather(in.ar, slot, tag, r, e, &fail_s, sum)) {
+            int64_t sum[4];
+            if (!ar_gather4(in.ar, slot, tag, r, e, &fail_s, sum)) {
                 if (!fail_s) atomicCAS(a.error, 0, kErrArTimeout);
                 fail_s = 1;
-                sum = 0;
+                sum[0] = sum[1] = sum[2] = sum[3] = 0;
             }
-            x = (int16_t)sat16((int32_t)in.resid[i] + round_mac(sum));
-            if (blockIdx.x == 0) in.hid_out[i] = x;
+            const uint2 rv = *reinterpret_cast<const uint2 *>(in.resid + i);
+            const int32_t y0 = sat16(lo16(rv.x) + round_mac(sum[0])), y1 = sat16(hi16(rv.x) + round_mac(sum[1]));
+            const int32_t y2 = sat16(lo16(rv.y) + round_mac(sum[2])), y3 = sat16(hi16(rv.y) + round_mac(sum[3]));
+            x.x = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+            x.y = ((uint32_t)y2 & 0xffffu) | ((uint32_t)y3 << 16);
+            if (blockIdx.x == 0) *reinterpret_cast<uint2 *>(in.hid_out + i) = x;
         }
-        xs[i] = x;
+        *reinterpret_cast<uint2 *>(xs + i) = x;
     }
     consumer_sync();
 }

@@ -84,27 +84,45 @@ static __device__ __forceinline__ uint64_t ar_load(const uint64_t *p) {
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-// Exact sum of element (r, e) over every rank's contribution to all-reduce
-// (slot, tag), read from this rank's exchange region.  Each word is waited for
-// at most ar.poll_limit polls; false when one did not arrive (or when *fail was
-// set by another thread of the block, so that a block gives up once).
-static __device__ __forceinline__ bool ar_gather(const ArPeers &ar, int slot, uint32_t tag, int r, int e,
-                                                 const volatile int *fail, int64_t &sum) {
+static __device__ __forceinline__ void ar_load2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Exact sums of elements (r, e..e+3) over every rank's contribution to
+// all-reduce (slot, tag), read from this rank's exchange region; e a multiple
+// of 4.  The 16-byte loads of up to four ranks are in flight before any tag is
+// checked (one round trip up to 4 ranks, two at 8).
+// Each word is waited for at most ar.poll_limit polls; false when one did not
+// arrive (or when *fail was set by another thread of the block, so that a
+// block gives up once).
+static __device__ __forceinline__ bool ar_gather4(const ArPeers &ar, int slot, uint32_t tag, int r, int e,
+                                                  const volatile int *fail, int64_t (&sum)[4]) {
+    constexpr int PB = 4;  // ranks per round trip
     const uint64_t *words = reinterpret_cast<const uint64_t *>(ar.base[ar.me] + kArHeader);
-    uint64_t w[kMaxTp];
 #pragma unroll
-    for (int p = 0; p < kMaxTp; p++)
-        if (p < ar.n) w[p] = ar_load(words + ar_word_index(slot, p, r, ar.hidden, e));
-    sum = 0;
+    for (int j = 0; j < 4; j++) sum[j] = 0;
+    for (int p0 = 0; p0 < ar.n; p0 += PB) {
+        uint64_t w[PB][4];
 #pragma unroll
-    for (int p = 0; p < kMaxTp; p++) {
-        if (p >= ar.n) break;
-        for (uint32_t it = 0; (uint32_t)(w[p] & 0xffffu) != tag; it++) {
-            if (it >= ar.poll_limit || *fail) return false;
-            __nanosleep(64);
-            w[p] = ar_load(words + ar_word_index(slot, p, r, ar.hidden, e));
+        for (int b = 0; b < PB; b++)
+            if (p0 + b < ar.n) {
+                const uint64_t *q = words + ar_word_index(slot, p0 + b, r, ar.hidden, e);
+                ar_load2(q, w[b][0], w[b][1]);
+                ar_load2(q + 2, w[b][2], w[b][3]);
+            }
+#pragma unroll
+        for (int b = 0; b < PB; b++) {
+            if (p0 + b >= ar.n) break;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                for (uint32_t it = 0; (uint32_t)(w[b][j] & 0xffffu) != tag; it++) {
+                    if (it >= ar.poll_limit || *fail) return false;
+                    __nanosleep(64);
+                    const uint64_t *q = words + ar_word_index(slot, p0 + b, r, ar.hidden, e + (j & ~1));
+                    ar_load2(q, w[b][j & ~1], w[b][j | 1]);
+                }
+                sum[j] += ar_value(w[b][j]);
+            }
         }
-        sum += ar_value(w[p]);
     }
     return true;
 }

@@ -87,21 +87,22 @@ __global__ void __launch_bounds__(256) k_ar_finish(const ArFinishArgs a) {
     const Step st = *a.step;
     const uint32_t n = st.ar_base + a.ar_off;
     const int H = a.ar.hidden;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);  // 4 consecutive elements (H % 8 == 0)
     if (i >= st.rows * H) return;
-    int64_t sum;
-    if (!ar_gather(a.ar, (int)(n & 1u), ar_tag(n), i / H, i % H, &fail_s, sum)) {
+    int64_t sum[4];
+    if (!ar_gather4(a.ar, (int)(n & 1u), ar_tag(n), i / H, i % H, &fail_s, sum)) {
         if (!fail_s) atomicCAS(a.error, 0, kErrArTimeout);
         fail_s = 1;
-        sum = 0;
+        sum[0] = sum[1] = sum[2] = sum[3] = 0;
     }
-    a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(sum));
+#pragma unroll
+    for (int j = 0; j < 4; j++) a.out[i + j] = (int16_t)sat16((int32_t)a.resid[i + j] + round_mac(sum[j]));
 }
 
 cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s) {
     ArFinishArgs c = a;
     void *args[] = {&c};
-    return launch_pdl((const void *)k_ar_finish, dim3((kMaxRows * a.ar.hidden + 255) / 256), dim3(256), args, s);
+    return launch_pdl((const void *)k_ar_finish, dim3((kMaxRows * a.ar.hidden / 4 + 255) / 256), dim3(256), args, s);
 }
 
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {

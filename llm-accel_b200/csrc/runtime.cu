@@ -65,11 +65,13 @@ struct llmx_ctx {
     cudaStream_t stream = nullptr;
     // geometry of this rank
     int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, tpc_max = 0;
-    // 16-CTA attention clusters when rows x local heads x 16 CTAs fill at most half of
-    // the SMs and the context can exceed 16 tiles (tensor-parallel ranks of 4 or 2
-    // heads; measured at context 2049: 14.5 -> 11.0 us, no gain at 8 heads)
+    // 16-CTA attention clusters when rows x local heads x 16 CTAs fit in one wave
+    // and the context can exceed 16 tiles (tensor-parallel ranks of 8, 4 or 2
+    // heads; measured at context 2049 with 4 heads: 14.5 -> 11.0 us; 16 heads,
+    // 256 CTAs, oversubscribe the SMs and stay on 8-CTA clusters)
     int tpc_max_wide = 0;
     bool attn_wide = false;
+    int attn_wide_div = 1;  // wide clusters while rows x heads x 16 CTAs <= SMs / div (LLMX_ATTN_WIDE_DIV)
     // weights: per layer [QKV | O | GU | D] words
     size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
     uint32_t *wbuf = nullptr;
@@ -97,7 +99,11 @@ struct llmx_ctx {
     // all-reduces enqueued so far (the same count on every rank); a call's first
     // all-reduce number reaches the kernels in the step record
     uint32_t ar_count = 0;
-    char *probe_region = nullptr;  // llmx_selftest_ar_timeout: an exchange region nobody writes
+    char *probe_region = nullptr;
+    // blocks of at most this many rows finish a peer all-reduce in the next
+    // projection's prologue (every CTA reads all rows' words); larger blocks
+    // use the finishing kernel once (LLMX_AR_FUSE_ROWS)
+    int ar_fuse_rows = 2;  // llmx_selftest_ar_timeout: an exchange region nobody writes
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -232,7 +238,7 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
 
 // Cluster size of an attention launch of `rows` rows.
 void pick_attn_cluster(const llmx_ctx *c, AttnArgs &t, uint32_t rows) {
-    if (c->attn_wide && 2 * (int)rows * c->hq * kClusterWide <= c->nsm) {
+    if (c->attn_wide && c->attn_wide_div * (int)rows * c->hq * kClusterWide <= c->nsm) {
         t.cluster = kClusterWide;
         t.tpc_max = c->tpc_max_wide;
     }
@@ -310,7 +316,7 @@ void take_input(llmx_ctx *c, ProjArgs &a, PendingAr &pend) {
 int after_partial(llmx_ctx *c, uint32_t rows, uint32_t &ar_next, int16_t *out, const int16_t *resid, bool fuse,
                   PendingAr &pend) {
     const uint32_t off = ar_next++;
-    if (fuse && c->ar.n > 1) {
+    if (fuse && c->ar.n > 1 && (int)rows <= c->ar_fuse_rows) {
         pend.active = true;
         pend.off = off;
         pend.resid = resid;
@@ -598,6 +604,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
+    c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
     auto bail = [&](int code) {
         release(c);
         return code;
@@ -615,7 +622,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
     // LLMX_ATTN_WIDE=0 keeps 8-CTA clusters everywhere
-    if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && 2 * c->hq * kClusterWide <= c->nsm &&
+    c->attn_wide_div = env_int("LLMX_ATTN_WIDE_DIV", 1, 1, 8);
+    if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && c->attn_wide_div * c->hq * kClusterWide <= c->nsm &&
         env_int("LLMX_ATTN_WIDE", 1, 0, 1) == 1) {
         e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide), kClusterWide);
         if (e == cudaSuccess) c->attn_wide = true;
