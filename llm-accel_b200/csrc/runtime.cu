@@ -99,11 +99,11 @@ struct llmx_ctx {
     // all-reduces enqueued so far (the same count on every rank); a call's first
     // all-reduce number reaches the kernels in the step record
     uint32_t ar_count = 0;
-    char *probe_region = nullptr;
+    char *probe_region = nullptr;  // llmx_selftest_ar_timeout: an exchange region nobody writes
     // blocks of at most this many rows finish a peer all-reduce in the next
     // projection's prologue (every CTA reads all rows' words); larger blocks
     // use the finishing kernel once (LLMX_AR_FUSE_ROWS)
-    int ar_fuse_rows = 2;  // llmx_selftest_ar_timeout: an exchange region nobody writes
+    int ar_fuse_rows = 2;
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
