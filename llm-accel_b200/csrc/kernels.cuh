@@ -93,6 +93,45 @@ struct ProjArgs {
     int row0;            // first row of this launch (x / out / resid already offset)
 };
 
+// Tensor-core projection of blocks of 3..8 rows (mma_proj.cu): weights in
+// "items" of 128 output rows x 128 inputs, high and low byte planes in the
+// tensor cores' K-major core-matrix order (k_pack_mma).
+constexpr int kMmaItemBytes = 2 * 128 * 128;
+struct MmaArgs {
+    const uint8_t *w;    // items of this projection, tile-major then K-chunk
+    int K;               // input features (<= C * 128)
+    int C;               // K-chunks of 128 inputs
+    int T;               // tiles of 128 output rows
+    int n_out;           // valid output units (EPI_RESID / PARTIAL: rows; EPI_SILU: FFN columns)
+    const int16_t *x;    // input rows [kMaxRows][K]
+    const int16_t *norm; // RMSNorm weights [K] (nullptr: none)
+    int32_t inv_elems, inv_rms_const;
+    const Step *step;
+    int16_t *out;
+    int out_stride;
+    const int16_t *resid;
+    int64_t *partial;
+    const int16_t *etab;
+    int16_t *kc, *vc;    // EPI_QKV: this layer's caches [kv_heads][max_seq][128]
+    const int16_t *rope; // [max_seq][128]
+    int q_tiles;         // EPI_QKV: tiles (heads) of Q; then kv_tiles of K, kv_tiles of V
+    int kv_tiles;
+    int max_seq;
+    ArPeers ar;          // EPI_PARTIAL with ar.n > 1: push the sums to every rank
+    uint32_t ar_off;
+    int64_t *scratch;    // [grid][2][kMaxRows][128] partial sums of shared tiles
+    int *tile_cnt;       // [T] arrivals at shared tiles (zero between launches)
+    int stages;          // ring stages of kMmaItemBytes
+    int max_items;       // items of the largest CTA range (activation slots)
+    int *error;
+};
+cudaError_t launch_mma_proj(const MmaArgs &a, int epi, int grid, cudaStream_t s);
+cudaError_t mma_configure(int max_smem_bytes);
+size_t mma_smem_bytes(int stages, int max_items);
+int mma_stages(int max_items, int max_smem);
+cudaError_t launch_pack_mma(const int16_t *dense, int ld, int col0, int K, int C, const int32_t *rows_of, int T,
+                            uint8_t *dst, cudaStream_t s);
+
 // CTAs per (row, query head) attention cluster: 8, or 16 (a non-portable size
 // B200 supports) when few heads leave most SMs idle, so that the contexts
 // longer than 16 tiles are spread 3 tiles per CTA instead of 5.

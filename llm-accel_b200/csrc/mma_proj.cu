@@ -1,0 +1,514 @@
+// Projection kernel for blocks of 3..8 rows on the fifth-generation tensor
+// cores (tcgen05.mma kind::i8, accumulators in tensor memory).
+//
+// Reference arithmetic: the exact int16 x int16 sum of the 8x64 fused MAC
+// engine, rounded twice (kernel/mm_stream_8x64_fused_mac.cpp:11-22,89-96,
+// 138-205; kernel/compute_core_8x64_unified.cpp:10-39; golden_projection
+// host/host_qwen_8x64.cpp:3105-3142).
+//
+// Exactness.  Split every int16 into a signed high byte and an unsigned low
+// byte, w = 256*wh + wl and x = 256*xh + xl.  Then
+//   sum w*x = 65536*sum(wh*xh) + 256*(sum(wh*xl) + sum(wl*xh)) + sum(wl*xl)
+// and each of the four byte sums is an int8 (s8/u8) tensor-core contraction
+// with an int32 accumulator that cannot overflow for K <= 11008:
+// |wh*xh| <= 2^14, |wh*xl| <= 128*255, wl*xl <= 255^2 = 65025 and
+// 65025 * 11008 < 2^31.  The four int32 sums are recombined in int64 by the
+// epilogue, so the result is the exact int64 dot product, as in the golden
+// model -- the operand widths of the reference fit the tensor cores exactly
+// once split into bytes.
+//
+// B200 mapping.  Weights are re-laid out at upload into "items": one item is
+// one tile of 128 output rows x 128 inputs, as two 16 KiB byte planes (high,
+// low) already in the tensor cores' K-major core-matrix order (8 rows x 16
+// bytes per 128-byte core matrix), so one 1-D bulk copy moves an item from HBM
+// into a shared-memory ring stage.  A projection is T tiles x C chunks of K;
+// the T*C items are split evenly and contiguously over the CTAs (stream-K), so
+// every CTA streams one contiguous byte range.  Per item the MMA thread issues
+// 4 K-steps x 4 byte-plane products (M = 128, N = 8 activation rows, K = 32
+// bytes) into one of two 32-column TMEM accumulator sets; four epilogue warps
+// read the sums with tcgen05.ld (one TMEM lane = one output row) and run the
+// fused epilogue of the path (RoPE + KV append, SiLU x up, residual, or the
+// tensor-parallel partial sums).  A tile shared by two or more CTAs is
+// finished by the last one to arrive: the others leave exact int64 partial
+// sums in a scratch slot and count themselves in; nobody waits for anybody.
+#include <cuda_runtime.h>
+
+#include "device_util.cuh"
+#include "fixed.cuh"
+#include "kernels.cuh"
+#include "gemv_common.cuh"
+
+namespace llmx {
+
+constexpr int kMmaThreads = 6 * 32;  // warp 0: TMEM + MMA issue, warp 1: weight producer, warps 2-5: epilogue
+constexpr int kTmemCols = 64;        // two accumulator sets x {hh, hl, lh, ll} x 8 rows
+constexpr int kMmaHdr = 1024;        // barriers and flags at the start of dynamic shared memory
+constexpr int kMmaMaxStages = 8;
+
+// ---- tcgen05 primitives -----------------------------------------------------
+// Shared-memory matrix descriptor, K-major, no swizzle: start address, LBO =
+// byte distance between the two 16-byte core matrices along K of one MMA
+// K-step, SBO = byte distance between 8-row core-matrix groups; version 1.
+static __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+           (1ull << 46);
+}
+// Instruction descriptor, kind::i8: int32 accumulator, A and B K-major,
+// M = 128, N = 8; a_signed / b_signed select s8 (1) or u8 (0).
+static __host__ __device__ constexpr uint32_t umma_idesc_i8(int a_signed, int b_signed) {
+    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
+}
+static __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// Arrive on an mbarrier once every tcgen05 operation this thread issued so far has completed.
+static __device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+static __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+static __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// 32 consecutive TMEM columns of this warp's 32 lanes (lane quarter in taddr bits 16+).
+static __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+static __device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Item range of CTA b: [first_item(b), first_item(b + 1)).
+static __host__ __device__ __forceinline__ int first_item(int b, int items, int grid) {
+    return (int)((int64_t)items * b / grid);
+}
+// CTA whose range holds item i.
+static __device__ __forceinline__ int cta_of_item(int i, int items, int grid) {
+    int b = (int)(((int64_t)i * grid) / items);
+    while (b + 1 < grid && first_item(b + 1, items, grid) <= i) b++;
+    while (b > 0 && first_item(b, items, grid) > i) b--;
+    return b;
+}
+
+// Activation rows -> the byte planes of every item chunk this CTA needs
+// (slot j = chunk of item w0 + j): RMS-normalised when a norm row is given.
+// Slot layout (2 KiB): high plane then low plane, each 8 rows x 128 bytes in
+// core-matrix order (16-byte column group kc at kc * 128, row r at r * 16).
+static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n, int rows, int tid, int T,
+                                      int32_t *inv_s, int64_t *red) {
+    const int K = a.K;
+    if (a.norm != nullptr) {
+        if (a.inv_elems == 0) {
+            if (tid < kMaxRows) inv_s[tid] = a.inv_rms_const;
+        } else {  // general RMSNorm: full-row sums of squares (stream_rmsnorm compute_stream.cpp:242-283)
+            for (int r = 0; r < kMaxRows; r++) {
+                int64_t part = 0;
+                if (r < rows)
+                    for (int i = tid; i < K; i += T) {
+                        const int32_t v = a.x[(size_t)r * K + i];
+                        part += (int64_t)v * v;
+                    }
+                for (int o = 16; o >= 1; o >>= 1) part += shfl_xor64(part, o);
+                if ((tid & 31) == 0) red[r * 8 + (tid >> 5)] = part;
+            }
+            named_sync(2, T);
+            if (tid < kMaxRows) {
+                int64_t sum = 0;
+                for (int w = 0; w < T / 32; w++) sum += red[tid * 8 + w];
+                inv_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
+            }
+        }
+        named_sync(2, T);
+    }
+    // one 16-element group (row r, column group kc of the chunk) per step
+    for (int u = tid; u < n * kMaxRows * 8; u += T) {
+        const int j = u / (kMaxRows * 8), rem = u - j * (kMaxRows * 8), r = rem >> 3, kc = rem & 7;
+        const int c = (w0 + j) % a.C;
+        const int col = c * 128 + kc * 16;
+        int32_t v[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++) v[q] = 0;
+        if (r < rows && col < K) {
+            // K is a multiple of 8, so a 16-column group is whole or half present
+            const uint4 *xp = reinterpret_cast<const uint4 *>(a.x + (size_t)r * K + col);
+            const int nv = min(2, (K - col) >> 3);
+            for (int h = 0; h < nv; h++) {
+                const uint4 xv = xp[h];
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    v[h * 8 + 2 * q] = lo16(xw[q]);
+                    v[h * 8 + 2 * q + 1] = hi16(xw[q]);
+                }
+            }
+            if (a.norm != nullptr) {
+                const int64_t inv = inv_s[r];
+                for (int q = 0; q < 8 * nv; q++)
+                    v[q] = sat16(rnd((int64_t)v[q] * inv * a.norm[col + q], 16));
+            }
+        }
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            hw[q] = lw[q] = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const uint32_t x = (uint32_t)v[4 * q + b];
+                hw[q] |= ((x >> 8) & 0xffu) << (8 * b);
+                lw[q] |= (x & 0xffu) << (8 * b);
+            }
+        }
+        char *slot = bsl + (size_t)j * 2048 + kc * 128 + r * 16;
+        *reinterpret_cast<uint4 *>(slot) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(slot + 1024) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+}
+
+// Final epilogue of one tile: thread m (TMEM lane) holds the exact sums of
+// tile row m for the 8 activation rows.
+template <int EPI>
+static __device__ void mma_epilogue(const MmaArgs &a, const Step &st, int t, int m, const int64_t (&S)[kMaxRows],
+                                    int32_t *ys) {
+    const int rows = st.rows;
+    if constexpr (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
+        const int o = t * 128 + m;
+        if (o >= a.n_out) return;
+        if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+            for (int r = 0; r < kMaxRows; r++)
+                if (r < rows) {
+                    const size_t i = (size_t)r * a.out_stride + o;
+                    a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(S[r]));
+                }
+        } else if (a.ar.n > 1) {  // tensor parallel: straight into every rank's exchange region
+            const uint32_t n = st.ar_base + a.ar_off;
+#pragma unroll
+            for (int r = 0; r < kMaxRows; r++)
+                if (r < rows) {
+                    const size_t w = ar_word_index((int)(n & 1u), a.ar.me, r, a.ar.hidden, o);
+                    const uint64_t word = ar_pack(S[r], ar_tag(n));
+                    for (int p = 0; p < a.ar.n; p++)
+                        ar_store(reinterpret_cast<uint64_t *>(a.ar.base[p] + kArHeader) + w, word);
+                }
+        } else {
+#pragma unroll
+            for (int r = 0; r < kMaxRows; r++)
+                if (r < rows) a.partial[(size_t)r * a.out_stride + o] = S[r];
+        }
+    } else {
+    // pair epilogues: rows m and m + 64 of the tile form one unit
+#pragma unroll
+    for (int r = 0; r < kMaxRows; r++) ys[r * 128 + m] = round_mac(S[r]);
+    named_sync(3, 128);
+    if (m < 64) {
+        if constexpr (EPI == EPI_SILU) {
+            const int u = t * 64 + m;  // FFN column of this rank
+            if (u < a.n_out)
+                for (int r = 0; r < rows; r++)
+                    a.out[(size_t)r * a.out_stride + u] = (int16_t)silu_mul(ys[r * 128 + m], ys[r * 128 + m + 64], a.etab);
+        } else {  // EPI_QKV: tile = one head (q heads of this rank, then K heads, then V heads)
+            const int half = 64;
+            for (int r = 0; r < rows; r++) {
+                const int pos = st.position + r;
+                const int32_t y0 = ys[r * 128 + m], y1 = ys[r * 128 + m + half];
+                if (t < a.q_tiles + a.kv_tiles) {
+                    // RoPE rotate_fix16_pair_with_quantized_rope host:4765-4788
+                    const int64_t cs = a.rope[(size_t)pos * 128 + m], sn = a.rope[(size_t)pos * 128 + half + m];
+                    const int16_t z0 = (int16_t)sat16(rnd((int64_t)y0 * cs - (int64_t)y1 * sn, 8));
+                    const int16_t z1 = (int16_t)sat16(rnd((int64_t)y1 * cs + (int64_t)y0 * sn, 8));
+                    int16_t *dst = t < a.q_tiles ? a.out + (size_t)r * a.out_stride + (size_t)t * 128
+                                                 : a.kc + ((size_t)(t - a.q_tiles) * a.max_seq + pos) * 128;
+                    dst[m] = z0;
+                    dst[m + half] = z1;
+                } else {
+                    int16_t *dst = a.vc + ((size_t)(t - a.q_tiles - a.kv_tiles) * a.max_seq + pos) * 128;
+                    dst[m] = (int16_t)y0;
+                    dst[m + half] = (int16_t)y1;
+                }
+            }
+        }
+    }
+    named_sync(3, 128);  // ys free for the next tile
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
+    extern __shared__ __align__(1024) char smem[];
+    // header: barriers, flags and the staging reduction (kMmaHdr bytes)
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmaMaxStages]
+    uint64_t *empty = full + kMmaMaxStages;               // [kMmaMaxStages]
+    uint64_t *tfull = empty + kMmaMaxStages;              // [2] accumulator set b ready for the epilogue
+    uint64_t *tempty = tfull + 2;                         // [2] accumulator set b read out
+    uint64_t *done = tempty + 2;                          // every MMA of the CTA completed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    int *last_s = reinterpret_cast<int *>(tmem_slot + 1);
+    int *fail_s = last_s + 1;                              // [2][4] per-tile wait outcome of each epilogue warp
+    int32_t *inv_s = fail_s + 8;                           // [8]
+    int64_t *red = reinterpret_cast<int64_t *>(smem + 512);  // [8][8]
+    char *ring = smem + kMmaHdr;
+    const int S = a.stages;
+    char *bsl = ring + (size_t)S * kMmaItemBytes;
+    int32_t *ys = reinterpret_cast<int32_t *>(bsl + (size_t)a.max_items * 2048);  // [8][128]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int items = a.T * a.C;
+    const int w0 = first_item(blockIdx.x, items, gridDim.x), w1 = first_item(blockIdx.x + 1, items, gridDim.x);
+    const int n = w1 - w0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);  // one tcgen05.commit per consumed item
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(tfull + b, 1);
+            mbar_init(tempty + b, 128);  // every epilogue thread
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 1) {  // ---------------- weight producer --------------------------------
+        if (lane == 0) {
+            const uint64_t policy = evict_first_policy();
+            const char *src = reinterpret_cast<const char *>(a.w) + (size_t)w0 * kMmaItemBytes;
+            bool ok = true;
+            int issued = 0;
+            for (int j = 0; j < n; j++) {
+                const int s = j % S;
+                if (j >= S && !mbar_wait(empty + s, ((j / S) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(full + s, kMmaItemBytes);
+                bulk_g2s_hint(ring + (size_t)s * kMmaItemBytes, src + (size_t)j * kMmaItemBytes, kMmaItemBytes,
+                              full + s, policy);
+                issued = j + 1;
+                if (j == S - 1) pdl_wait();  // ring primed before waiting on the previous kernel
+            }
+            if (n < S) pdl_wait();
+            if (!ok) {
+                atomicExch(a.error, 1);
+                for (int s = 0; s < S && s < issued; s++) {
+                    const int last = s + ((issued - 1 - s) / S) * S;
+                    (void)mbar_wait(full + s, (last / S) & 1);
+                }
+            }
+        }
+    } else {  // ---------------- warps 0, 2-5: activations, then MMA / epilogue ---------
+        const int tid = warp == 0 ? lane : threadIdx.x - 32;  // 0..159
+        pdl_wait();
+        pdl_trigger();
+        const Step st = *a.step;
+        mma_stage_rows(a, bsl, w0, n, st.rows, tid, 160, inv_s, red);
+        named_sync(1, 160);
+
+        if (warp == 0) {  // ---------------- MMA issue (one thread) ----------------------
+            if (lane == 0) {
+                constexpr uint32_t kSS = umma_idesc_i8(1, 1), kSU = umma_idesc_i8(1, 0), kUS = umma_idesc_i8(0, 1),
+                                   kUU = umma_idesc_i8(0, 0);
+                int tiles_done = 0;
+                bool ok = true;
+                for (int j = 0; j < n && ok; j++) {
+                    const int i = w0 + j, c = i % a.C;
+                    const bool first = j == 0 || c == 0, last = j == n - 1 || c == a.C - 1;
+                    const int b = tiles_done & 1;
+                    if (first && tiles_done >= 2 && !mbar_wait(tempty + b, ((tiles_done >> 1) - 1) & 1)) ok = false;
+                    if (ok && !mbar_wait(full + j % S, (j / S) & 1)) ok = false;
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(ring + (size_t)(j % S) * kMmaItemBytes), al = ah + 16384;
+                    const uint32_t bh = smem_u32(bsl + (size_t)j * 2048), bl = bh + 1024;
+                    const uint32_t d = tmem + (uint32_t)b * 32;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {  // 32-byte K-steps of the 128-byte chunk
+                        const uint32_t acc = (first && k == 0) ? 0u : 1u;
+                        const uint64_t dah = umma_desc(ah + k * 256, 128, 1024), dal = umma_desc(al + k * 256, 128, 1024);
+                        const uint64_t dbh = umma_desc(bh + k * 256, 128, 1024), dbl = umma_desc(bl + k * 256, 128, 1024);
+                        umma_i8(d + 0, dah, dbh, kSS, acc);
+                        umma_i8(d + 8, dah, dbl, kSU, acc);
+                        umma_i8(d + 16, dal, dbh, kUS, acc);
+                        umma_i8(d + 24, dal, dbl, kUU, acc);
+                    }
+                    umma_commit(empty + j % S);  // ring stage free once these MMAs are done
+                    if (last) {
+                        umma_commit(tfull + b);
+                        tiles_done++;
+                    }
+                }
+                if (!ok) atomicExch(a.error, 2);  // the epilogue finds the flag and stops waiting
+                // the accumulators are released only after every issued MMA has completed
+                umma_commit(done);
+                if (!mbar_wait(done, 0)) atomicExch(a.error, 2);
+            }
+            __syncwarp();
+        } else {  // ---------------- epilogue warps 2-5 -----------------------------------
+            const int q = warp & 3, m = q * 32 + lane;  // TMEM lane quarter of this warp, tile row
+            const int t0 = w0 / a.C, t1 = n > 0 ? (w1 - 1) / a.C : t0 - 1;
+            int tiles_done = 0;
+            for (int t = t0; t <= t1; t++, tiles_done++) {
+                const int b = tiles_done & 1;
+                // the four warps decide together whether to go on (they meet at named barriers)
+                const bool okw = mbar_wait_err(tfull + b, (tiles_done >> 1) & 1, a.error);
+                if (lane == 0) fail_s[b * 4 + q] = okw ? 0 : 1;
+                named_sync(3, 128);
+                if (fail_s[b * 4] | fail_s[b * 4 + 1] | fail_s[b * 4 + 2] | fail_s[b * 4 + 3]) {
+                    if (m == 0) atomicCAS(a.error, 0, 3);
+                    break;
+                }
+                tc_fence_after();
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * 32, v);
+                tc_fence_before();
+                mbar_arrive(tempty + b);
+                int64_t Sm[kMaxRows];
+#pragma unroll
+                for (int r = 0; r < kMaxRows; r++)
+                    Sm[r] = (int64_t)(int32_t)v[r] * 65536 +
+                            ((int64_t)(int32_t)v[8 + r] + (int64_t)(int32_t)v[16 + r]) * 256 + (int64_t)(int32_t)v[24 + r];
+                const int seg0 = max(w0, t * a.C), seg1 = min(w1, (t + 1) * a.C);
+                if (seg0 != t * a.C || seg1 != (t + 1) * a.C) {
+                    // shared tile: leave the partial sums, count in; the last CTA finishes it
+                    const int which = t == t0 ? 0 : 1;
+                    int64_t *slot = a.scratch + ((size_t)(blockIdx.x * 2 + which) * kMaxRows) * 128;
+#pragma unroll
+                    for (int r = 0; r < kMaxRows; r++) slot[r * 128 + m] = Sm[r];
+                    __threadfence();
+                    named_sync(3, 128);
+                    const int b_lo = cta_of_item(t * a.C, items, gridDim.x);
+                    const int b_hi = cta_of_item((t + 1) * a.C - 1, items, gridDim.x);
+                    if (m == 0) *last_s = atomicAdd(a.tile_cnt + t, 1) == b_hi - b_lo;
+                    named_sync(3, 128);
+                    if (!*last_s) continue;
+                    __threadfence();
+                    for (int bb = b_lo; bb <= b_hi; bb++) {
+                        if (bb == (int)blockIdx.x) continue;
+                        const int wh = t == first_item(bb, items, gridDim.x) / a.C ? 0 : 1;
+                        const int64_t *o = a.scratch + ((size_t)(bb * 2 + wh) * kMaxRows) * 128;
+#pragma unroll
+                        for (int r = 0; r < kMaxRows; r++) Sm[r] += __ldcg(o + r * 128 + m);
+                    }
+                    if (m == 0) a.tile_cnt[t] = 0;  // ready for the next launch
+                }
+                mma_epilogue<EPI>(a, st, t, m, Sm, ys);
+            }
+        }
+    }
+    // every MMA has completed before the accumulators are released: the epilogue
+    // waited for each tile's commit, and an error path waits for the last one here
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+size_t mma_smem_bytes(int stages, int max_items) {
+    return kMmaHdr + (size_t)stages * kMmaItemBytes + (size_t)max_items * 2048 + (size_t)kMaxRows * 128 * 4;
+}
+
+// Ring depth that fits shared memory (2..kMaxStages stages).
+int mma_stages(int max_items, int max_smem) {
+    int s = 6 < kMmaMaxStages ? 6 : kMmaMaxStages;
+    while (s > 2 && mma_smem_bytes(s, max_items) > (size_t)max_smem) s--;
+    return mma_smem_bytes(s, max_items) <= (size_t)max_smem ? s : 0;
+}
+
+template <int EPI>
+static cudaError_t launch_mma_t(const MmaArgs &a, int grid, cudaStream_t st) {
+    MmaArgs c = a;
+    void *args[] = {&c};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = mma_smem_bytes(a.stages, a.max_items);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, (const void *)k_mma_proj<EPI>, args);
+}
+
+cudaError_t launch_mma_proj(const MmaArgs &a, int epi, int grid, cudaStream_t s) {
+    switch (epi) {
+    case EPI_QKV: return launch_mma_t<EPI_QKV>(a, grid, s);
+    case EPI_RESID: return launch_mma_t<EPI_RESID>(a, grid, s);
+    case EPI_SILU: return launch_mma_t<EPI_SILU>(a, grid, s);
+    default: return launch_mma_t<EPI_PARTIAL>(a, grid, s);
+    }
+}
+
+cudaError_t mma_configure(int max_smem_bytes) {
+    constexpr auto kAttr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(k_mma_proj<EPI_QKV>, kAttr, max_smem_bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_mma_proj<EPI_RESID>, kAttr, max_smem_bytes))) return e;
+    if ((e = cudaFuncSetAttribute(k_mma_proj<EPI_SILU>, kAttr, max_smem_bytes))) return e;
+    return cudaFuncSetAttribute(k_mma_proj<EPI_PARTIAL>, kAttr, max_smem_bytes);
+}
+
+// --------------------------------------------------------------------------
+// weight layout for the tensor-core path (model upload)
+// --------------------------------------------------------------------------
+// Item (t, c) = tile t (128 output rows; tile row m is dense row rows_of[t*128+m],
+// -1 = zero padding), K-chunk c (input columns col0 + c*128 .. +127, zero past K):
+// high-byte plane then low-byte plane, each with byte (m, k) at
+// ((m / 8) * 8 + k / 16) * 128 + (m % 8) * 16 + k % 16.
+__global__ void k_pack_mma(const int16_t *__restrict__ dense, int ld, int col0, int K, int C,
+                           const int32_t *__restrict__ rows_of, int T, uint8_t *__restrict__ dst) {
+    const size_t groups = (size_t)T * C * 2 * 128 * 8;  // 16-byte groups
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (size_t)gridDim.x * blockDim.x) {
+        const int kc = (int)(g & 7), m = (int)((g >> 3) & 127);
+        const size_t rest = g >> 10;
+        const int plane = (int)(rest & 1);
+        const size_t item = rest >> 1;
+        const int t = (int)(item / C), c = (int)(item - (size_t)t * C);
+        const int row = rows_of[t * 128 + m];
+        uint32_t w[4] = {0, 0, 0, 0};
+        for (int e = 0; e < 16; e++) {
+            const int col = c * 128 + kc * 16 + e;
+            uint32_t byte = 0;
+            if (row >= 0 && col < K) {
+                const uint32_t v = (uint16_t)dense[(size_t)row * ld + col0 + col];
+                byte = plane == 0 ? (v >> 8) : (v & 0xffu);
+            }
+            w[e >> 2] |= byte << (8 * (e & 3));
+        }
+        uint8_t *p = dst + item * kMmaItemBytes + (size_t)plane * 16384 + ((m >> 3) * 8 + kc) * 128 + (m & 7) * 16;
+        *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+cudaError_t launch_pack_mma(const int16_t *dense, int ld, int col0, int K, int C, const int32_t *rows_of, int T,
+                            uint8_t *dst, cudaStream_t s) {
+    const size_t groups = (size_t)T * C * 2 * 128 * 8;
+    int blocks = (int)std::min<size_t>((groups + 255) / 256, 65535 * 8);
+    k_pack_mma<<<blocks, 256, 0, s>>>(dense, ld, col0, K, C, rows_of, T, dst);
+    return cudaGetLastError();
+}
+
+}  // namespace llmx

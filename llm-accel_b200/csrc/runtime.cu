@@ -58,6 +58,13 @@ int rows_template(uint32_t rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <
 
 void llmx::set_last_error(const std::string &msg) { g_last_error = msg; }
 
+// Geometry of one projection in the tensor-core item layout.
+struct MmaGeom {
+    int T = 0, C = 0, K = 0, n_out = 0;
+    size_t offset = 0;  // bytes from the start of the layer's item blob
+    size_t items() const { return (size_t)T * C; }
+};
+
 struct llmx_ctx {
     llmx_shape s{};
     int dev = 0, rank = 0, size = 1, nsm = 148;
@@ -104,6 +111,17 @@ struct llmx_ctx {
     // projection's prologue (every CTA reads all rows' words); larger blocks
     // use the finishing kernel once (LLMX_AR_FUSE_ROWS)
     int ar_fuse_rows = 2;
+    // tensor-core projections (mma_proj.cu) for blocks of at least mma_min_rows
+    // rows: a second copy of every layer's weights in item layout, stream-K
+    // scratch and tile counters (LLMX_MMA=0 disables, LLMX_MMA_MIN_ROWS)
+    bool mma = false;
+    int mma_min_rows = 3;
+    MmaGeom mg[4]{};             // QKV, O, Gate/Up, Down of this rank
+    size_t mma_layer_bytes = 0;
+    uint8_t *mbuf = nullptr;
+    int64_t *mma_scratch = nullptr;
+    int *mma_cnt = nullptr;
+    int32_t *mma_rows[4] = {nullptr, nullptr, nullptr, nullptr};
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
     std::vector<bool> layer_loaded;
@@ -291,6 +309,10 @@ ProjArgs down_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in)
     return d;
 }
 
+enum { MP_QKV = 0, MP_O = 1, MP_GU = 2, MP_D = 3 };
+
+bool use_mma(const llmx_ctx *c, uint32_t rows) { return c->mma && (int)rows >= c->mma_min_rows; }
+
 // A peer all-reduce whose finishing step is still to come: its number within
 // the call, the residual to add and where the finished rows belong.
 struct PendingAr {
@@ -316,7 +338,7 @@ void take_input(llmx_ctx *c, ProjArgs &a, PendingAr &pend) {
 int after_partial(llmx_ctx *c, uint32_t rows, uint32_t &ar_next, int16_t *out, const int16_t *resid, bool fuse,
                   PendingAr &pend) {
     const uint32_t off = ar_next++;
-    if (fuse && c->ar.n > 1 && (int)rows <= c->ar_fuse_rows) {
+    if (fuse && c->ar.n > 1 && (int)rows <= c->ar_fuse_rows && !use_mma(c, rows)) {
         pend.active = true;
         pend.off = off;
         pend.resid = resid;
@@ -324,6 +346,49 @@ int after_partial(llmx_ctx *c, uint32_t rows, uint32_t &ar_next, int16_t *out, c
         return LLMX_OK;
     }
     return allreduce_resid(c, rows, off, out, resid);
+}
+
+// A projection on the tensor cores (mma_proj.cu); the dp2a arguments p carry
+// the epilogue's operands (inputs, outputs, residual, caches, tables).
+int launch_mma(llmx_ctx *c, const ProjArgs &p, int proj, uint32_t layer, int epi) {
+    const MmaGeom &g = c->mg[proj];
+    MmaArgs m{};
+    m.w = c->mbuf + (size_t)layer * c->mma_layer_bytes + g.offset;
+    m.K = g.K;
+    m.C = g.C;
+    m.T = g.T;
+    m.n_out = g.n_out;
+    m.x = p.x;
+    m.norm = p.norm;
+    m.inv_elems = p.inv_elems;
+    m.inv_rms_const = p.inv_rms_const;
+    m.step = c->step;
+    m.out = p.out;
+    m.out_stride = p.out_stride;
+    m.resid = p.resid;
+    m.partial = p.partial;
+    m.etab = p.etab;
+    m.kc = p.kc;
+    m.vc = p.vc;
+    m.rope = p.rope;
+    m.q_tiles = c->hq;
+    m.kv_tiles = c->s.kv_heads;
+    m.max_seq = c->s.max_seq;
+    m.ar = p.ar;
+    m.ar_off = p.ar_off;
+    m.scratch = c->mma_scratch;
+    m.tile_cnt = c->mma_cnt;
+    m.error = c->err;
+    const int items = (int)g.items();
+    const int grid = std::min(c->nsm, items);
+    m.max_items = (items + grid - 1) / grid;
+    m.stages = mma_stages(m.max_items, kProjSmem);
+    if (m.stages < 2) {
+        g_last_error = "tensor-core projection: the item ring does not fit shared memory";
+        return LLMX_ERR_UNSUPPORTED;
+    }
+    CK(launch_mma_proj(m, epi, grid, c->stream));
+    return LLMX_OK;
 }
 
 // Enqueue the kernels of one coarse task on the context stream.  ar_next counts
@@ -339,16 +404,26 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         ProjArgs a = qkv_args(c, layer, in);
         take_input(c, a, pend);
-        set_stages(c, a, EPI_QKV, rt);
-        CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
+        if (use_mma(c, rows)) {
+            const int rc = launch_mma(c, a, MP_QKV, layer, EPI_QKV);
+            if (rc) return rc;
+        } else {
+            set_stages(c, a, EPI_QKV, rt);
+            CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
+        }
         AttnArgs t = attn_args(c, layer);
         pick_attn_cluster(c, t, rows);
         if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
         CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
         o.ar_off = ar_next;
-        set_stages(c, o, ge, rt);
-        CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
+        if (use_mma(c, rows)) {
+            const int rc = launch_mma(c, o, MP_O, layer, ge);
+            if (rc) return rc;
+        } else {
+            set_stages(c, o, ge, rt);
+            CK(launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream));
+        }
         c->launches += 3;
         if (c->size > 1) return after_partial(c, rows, ar_next, out, in, fuse, pend);
         return LLMX_OK;
@@ -356,11 +431,16 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     if (op == LLMX_OP_FFN_SUBLAYER) {
         ProjArgs g = gu_args(c, layer, in);
         take_input(c, g, pend);
-        set_stages(c, g, EPI_SILU, rt);
-        CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
         ProjArgs d = down_args(c, layer, out, in);
         d.ar_off = ar_next;
-        if (rt == 8 && c->size == 1) {
+        if (use_mma(c, rows)) {
+            int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
+            if (!rc) rc = launch_mma(c, d, MP_D, layer, ge);
+            if (rc) return rc;
+            c->launches += 2;
+        } else if (rt == 8 && c->size == 1) {
+            set_stages(c, g, EPI_SILU, rt);
+            CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
             // an 8-row block as two 4-row launches: 8 FFN-wide activation rows would
             // fill shared memory and starve the weight ring; 4 rows leave it room
             for (int half = 0; half < 2; half++) {
@@ -374,6 +454,8 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
             }
             c->launches += 3;
         } else {
+            set_stages(c, g, EPI_SILU, rt);
+            CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
             set_stages(c, d, ge, rt);
             CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
             c->launches += 2;
@@ -651,6 +733,57 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->step, 1)) || (rc = dalloc(c, &c->err, 1)))
         return bail(rc);
 
+    // tensor-core projections for blocks of mma_min_rows..8 rows: QKV tiles are
+    // heads, so head_dim must be 128 (every Qwen profile); LLMX_MMA=0 disables
+    c->mma_min_rows = env_int("LLMX_MMA_MIN_ROWS", 3, 1, 9);
+    if (hd == 128 && env_int("LLMX_MMA", 1, 0, 1) == 1) {
+        auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
+        MmaGeom *g = c->mg;
+        const int Hi = (int)H;
+        g[MP_QKV].T = hq + 2 * s.kv_heads, g[MP_QKV].C = cdiv(Hi, 128), g[MP_QKV].K = Hi;
+        g[MP_QKV].n_out = g[MP_QKV].T * 128;
+        g[MP_O].T = cdiv(Hi, 128), g[MP_O].C = cdiv(c->Hq, 128), g[MP_O].K = c->Hq, g[MP_O].n_out = Hi;
+        g[MP_GU].T = cdiv(c->Il, 64), g[MP_GU].C = cdiv(Hi, 128), g[MP_GU].K = Hi, g[MP_GU].n_out = c->Il;
+        g[MP_D].T = cdiv(Hi, 128), g[MP_D].C = cdiv(c->Il, 128), g[MP_D].K = c->Il, g[MP_D].n_out = Hi;
+        size_t off = 0;
+        int tmax = 0;
+        for (int p = 0; p < 4; p++) {
+            g[p].offset = off;
+            off += g[p].items() * kMmaItemBytes;
+            tmax = std::max(tmax, g[p].T);
+        }
+        c->mma_layer_bytes = off;
+        if ((rc = dalloc(c, &c->mbuf, off * s.layers)) ||
+            (rc = dalloc(c, &c->mma_scratch, (size_t)c->nsm * 2 * kMaxRows * 128)) ||
+            (rc = dalloc(c, &c->mma_cnt, (size_t)tmax)))
+            return bail(rc);
+        // tile row -> dense row of each projection's source matrix (-1: zero padding)
+        for (int p = 0; p < 4; p++) {
+            std::vector<int32_t> rows((size_t)g[p].T * 128, -1);
+            for (int t = 0; t < g[p].T; t++)
+                for (int m = 0; m < 128; m++) {
+                    int32_t r = -1;
+                    if (p == MP_QKV) {
+                        const int kvh = t - hq;
+                        r = t < hq ? (c->h0 + t) * 128 + m
+                                   : (kvh < s.kv_heads ? Hi + kvh * 128 + m : Hi + c->KV + (kvh - s.kv_heads) * 128 + m);
+                    } else if (p == MP_GU) {
+                        const int u = t * 64 + (m & 63);
+                        if (u < c->Il) r = m < 64 ? c->c0 + u : s.inter + c->c0 + u;
+                    } else if (t * 128 + m < Hi) {
+                        r = t * 128 + m;
+                    }
+                    rows[(size_t)t * 128 + m] = r;
+                }
+            if ((rc = dalloc(c, &c->mma_rows[p], rows.size()))) return bail(rc);
+            e = cudaMemcpy(c->mma_rows[p], rows.data(), rows.size() * 4, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return bail(fail_cuda(e, "tile row upload"));
+        }
+        e = mma_configure(kProjSmem);
+        if (e != cudaSuccess) return bail(fail_cuda(e, "mma_configure"));
+        c->mma = true;
+    }
+
     // slot -> dense row tables of the pair-interleaved layout
     {
         std::vector<int32_t> t;
@@ -728,6 +861,18 @@ int llmx_upload_layer(llmx_ctx *c, uint32_t layer, const int16_t *dense) {
     CK(launch_pack_pairs(c->staging + off[4], H, 0, H, c->slot_gu, 2 * c->Il, w + c->w_qkv + c->w_o, c->stream));
     CK(launch_pack_pairs(c->staging + off[6], s.inter, c->c0, c->Il, c->slot_d, H,
                          w + c->w_qkv + c->w_o + c->w_gu, c->stream));
+    if (c->mma) {  // the tensor-core item layout of the same weights
+        uint8_t *mb = c->mbuf + (size_t)layer * c->mma_layer_bytes;
+        const MmaGeom *g = c->mg;
+        CK(launch_pack_mma(c->staging + off[0], H, 0, H, g[MP_QKV].C, c->mma_rows[MP_QKV], g[MP_QKV].T,
+                           mb + g[MP_QKV].offset, c->stream));
+        CK(launch_pack_mma(c->staging + off[3], H, c->h0 * c->hd, c->Hq, g[MP_O].C, c->mma_rows[MP_O], g[MP_O].T,
+                           mb + g[MP_O].offset, c->stream));
+        CK(launch_pack_mma(c->staging + off[4], H, 0, H, g[MP_GU].C, c->mma_rows[MP_GU], g[MP_GU].T,
+                           mb + g[MP_GU].offset, c->stream));
+        CK(launch_pack_mma(c->staging + off[6], s.inter, c->c0, c->Il, g[MP_D].C, c->mma_rows[MP_D], g[MP_D].T,
+                           mb + g[MP_D].offset, c->stream));
+    }
     CK(cudaStreamSynchronize(c->stream));
     c->layer_loaded[layer] = true;
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.first);
@@ -909,6 +1054,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         switch (kernel) {
         case LLMX_KERNEL_QKV: {
             ProjArgs a = qkv_args(c, layer, in);
+            if (use_mma(c, rows)) return launch_mma(c, a, MP_QKV, layer, EPI_QKV) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
@@ -921,17 +1067,20 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
             o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
+            if (use_mma(c, rows)) return launch_mma(c, o, MP_O, layer, ge) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, o, ge, rt);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
         }
         case LLMX_KERNEL_GATE_UP: {
             ProjArgs g = gu_args(c, layer, in);
+            if (use_mma(c, rows)) return launch_mma(c, g, MP_GU, layer, EPI_SILU) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, g, EPI_SILU, rt);
             return launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream);
         }
         case LLMX_KERNEL_DOWN: {
             ProjArgs d = down_args(c, layer, out, in);
             d.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
+            if (use_mma(c, rows)) return launch_mma(c, d, MP_D, layer, ge) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, d, ge, rt);
             return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
         }
