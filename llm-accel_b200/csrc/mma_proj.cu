@@ -131,47 +131,55 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
         }
         named_sync(2, T);
     }
-    // one 16-element group (row r, column group kc of the chunk) per step
-    for (int u = tid; u < n * kMaxRows * 8; u += T) {
-        const int j = u / (kMaxRows * 8), rem = u - j * (kMaxRows * 8), r = rem >> 3, kc = rem & 7;
-        const int c = (w0 + j) % a.C;
-        const int col = c * 128 + kc * 16;
-        int32_t v[16];
+    // one 16-element group (row r, column group kc of the chunk) per unit; the
+    // loads of kBatch units are all in flight before any is used
+    constexpr int kBatch = 4;
+    const int units = n * kMaxRows * 8;
+    for (int u0 = tid; u0 < units; u0 += kBatch * T) {
+        uint4 xv[kBatch][2], wv[kBatch][2];
 #pragma unroll
-        for (int q = 0; q < 16; q++) v[q] = 0;
-        if (r < rows && col < K) {
-            // K is a multiple of 8, so a 16-column group is whole or half present
-            const uint4 *xp = reinterpret_cast<const uint4 *>(a.x + (size_t)r * K + col);
-            const int nv = min(2, (K - col) >> 3);
-            for (int h = 0; h < nv; h++) {
-                const uint4 xv = xp[h];
-                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int k = 0; k < kBatch; k++) {
+            const int u = u0 + k * T;
+            const int j = u / (kMaxRows * 8), rem = u - j * (kMaxRows * 8), r = rem >> 3, kc = rem & 7;
+            const int col = ((w0 + j) % a.C) * 128 + kc * 16;
+            // K is a multiple of 8: a 16-column group is whole, half or not present
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    v[h * 8 + 2 * q] = lo16(xw[q]);
-                    v[h * 8 + 2 * q + 1] = hi16(xw[q]);
+            for (int h = 0; h < 2; h++) {
+                const bool in = u < units && r < rows && col + 8 * h < K;
+                xv[k][h] = in ? *reinterpret_cast<const uint4 *>(a.x + (size_t)r * K + col + 8 * h) : make_uint4(0, 0, 0, 0);
+                wv[k][h] = in && a.norm != nullptr ? *reinterpret_cast<const uint4 *>(a.norm + col + 8 * h)
+                                                   : make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; k++) {
+            const int u = u0 + k * T;
+            if (u >= units) break;
+            const int j = u / (kMaxRows * 8), rem = u - j * (kMaxRows * 8), r = rem >> 3, kc = rem & 7;
+            const int32_t inv = a.norm != nullptr ? inv_s[r] : 0;
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                uint32_t xw[4] = {xv[k][h].x, xv[k][h].y, xv[k][h].z, xv[k][h].w};
+                const uint32_t ww[4] = {wv[k][h].x, wv[k][h].y, wv[k][h].z, wv[k][h].w};
+                if (a.norm != nullptr) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {  // x * w fits 32 bits; one widening multiply by inv
+                        const int32_t y0 = sat16(rnd((int64_t)(lo16(xw[q]) * lo16(ww[q])) * inv, 16));
+                        const int32_t y1 = sat16(rnd((int64_t)(hi16(xw[q]) * hi16(ww[q])) * inv, 16));
+                        xw[q] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+                    }
                 }
+                // bytes of 4 consecutive int16 (two words): high bytes 1,3,5,7 and low bytes 0,2,4,6
+                hw[2 * h] = __byte_perm(xw[0], xw[1], 0x7531);
+                lw[2 * h] = __byte_perm(xw[0], xw[1], 0x6420);
+                hw[2 * h + 1] = __byte_perm(xw[2], xw[3], 0x7531);
+                lw[2 * h + 1] = __byte_perm(xw[2], xw[3], 0x6420);
             }
-            if (a.norm != nullptr) {
-                const int64_t inv = inv_s[r];
-                for (int q = 0; q < 8 * nv; q++)
-                    v[q] = sat16(rnd((int64_t)v[q] * inv * a.norm[col + q], 16));
-            }
+            char *slot = bsl + (size_t)j * 2048 + kc * 128 + r * 16;
+            *reinterpret_cast<uint4 *>(slot) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4 *>(slot + 1024) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            hw[q] = lw[q] = 0;
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const uint32_t x = (uint32_t)v[4 * q + b];
-                hw[q] |= ((x >> 8) & 0xffu) << (8 * b);
-                lw[q] |= (x & 0xffu) << (8 * b);
-            }
-        }
-        char *slot = bsl + (size_t)j * 2048 + kc * 128 + r * 16;
-        *reinterpret_cast<uint4 *>(slot) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4 *>(slot + 1024) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
 }
@@ -180,7 +188,7 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
 // tile row m for the 8 activation rows.
 template <int EPI>
 static __device__ void mma_epilogue(const MmaArgs &a, const Step &st, int t, int m, const int64_t (&S)[kMaxRows],
-                                    int32_t *ys) {
+                                    int32_t *ys, const int16_t *etab_s) {
     const int rows = st.rows;
     if constexpr (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
         const int o = t * 128 + m;
@@ -208,35 +216,50 @@ static __device__ void mma_epilogue(const MmaArgs &a, const Step &st, int t, int
                 if (r < rows) a.partial[(size_t)r * a.out_stride + o] = S[r];
         }
     } else {
-    // pair epilogues: rows m and m + 64 of the tile form one unit
+    // pair epilogues: rows m and m + 64 of the tile form one unit; thread m
+    // then finishes pair (m mod 64) for activation rows 4*(m / 64) .. +3
 #pragma unroll
     for (int r = 0; r < kMaxRows; r++) ys[r * 128 + m] = round_mac(S[r]);
     named_sync(3, 128);
-    if (m < 64) {
-        if constexpr (EPI == EPI_SILU) {
-            const int u = t * 64 + m;  // FFN column of this rank
-            if (u < a.n_out)
-                for (int r = 0; r < rows; r++)
-                    a.out[(size_t)r * a.out_stride + u] = (int16_t)silu_mul(ys[r * 128 + m], ys[r * 128 + m + 64], a.etab);
-        } else {  // EPI_QKV: tile = one head (q heads of this rank, then K heads, then V heads)
-            const int half = 64;
-            for (int r = 0; r < rows; r++) {
-                const int pos = st.position + r;
-                const int32_t y0 = ys[r * 128 + m], y1 = ys[r * 128 + m + half];
-                if (t < a.q_tiles + a.kv_tiles) {
-                    // RoPE rotate_fix16_pair_with_quantized_rope host:4765-4788
-                    const int64_t cs = a.rope[(size_t)pos * 128 + m], sn = a.rope[(size_t)pos * 128 + half + m];
-                    const int16_t z0 = (int16_t)sat16(rnd((int64_t)y0 * cs - (int64_t)y1 * sn, 8));
-                    const int16_t z1 = (int16_t)sat16(rnd((int64_t)y1 * cs + (int64_t)y0 * sn, 8));
-                    int16_t *dst = t < a.q_tiles ? a.out + (size_t)r * a.out_stride + (size_t)t * 128
-                                                 : a.kc + ((size_t)(t - a.q_tiles) * a.max_seq + pos) * 128;
-                    dst[m] = z0;
-                    dst[m + half] = z1;
-                } else {
-                    int16_t *dst = a.vc + ((size_t)(t - a.q_tiles - a.kv_tiles) * a.max_seq + pos) * 128;
-                    dst[m] = (int16_t)y0;
-                    dst[m + half] = (int16_t)y1;
-                }
+    const int p = m & 63, r0 = (m >> 6) * 4;
+    if constexpr (EPI == EPI_SILU) {
+        const int u = t * 64 + p;  // FFN column of this rank
+        if (u < a.n_out) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int r = r0 + k;
+                if (r < rows)
+                    a.out[(size_t)r * a.out_stride + u] = (int16_t)silu_mul(ys[r * 128 + p], ys[r * 128 + p + 64], etab_s);
+            }
+        }
+    } else {  // EPI_QKV: tile = one head (q heads of this rank, then K heads, then V heads)
+        constexpr int half = 64;
+        const bool rope = t < a.q_tiles + a.kv_tiles;
+        int64_t cs[4], sn[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {  // RoPE rows of every position first (independent loads)
+            const int pos = st.position + r0 + k;
+            cs[k] = rope && r0 + k < rows ? a.rope[(size_t)pos * 128 + p] : 0;
+            sn[k] = rope && r0 + k < rows ? a.rope[(size_t)pos * 128 + half + p] : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int r = r0 + k;
+            if (r >= rows) continue;
+            const int pos = st.position + r;
+            const int32_t y0 = ys[r * 128 + p], y1 = ys[r * 128 + p + half];
+            if (rope) {
+                // RoPE rotate_fix16_pair_with_quantized_rope host:4765-4788
+                const int16_t z0 = (int16_t)sat16(rnd((int64_t)y0 * cs[k] - (int64_t)y1 * sn[k], 8));
+                const int16_t z1 = (int16_t)sat16(rnd((int64_t)y1 * cs[k] + (int64_t)y0 * sn[k], 8));
+                int16_t *dst = t < a.q_tiles ? a.out + (size_t)r * a.out_stride + (size_t)t * 128
+                                             : a.kc + ((size_t)(t - a.q_tiles) * a.max_seq + pos) * 128;
+                dst[p] = z0;
+                dst[p + half] = z1;
+            } else {
+                int16_t *dst = a.vc + ((size_t)(t - a.q_tiles - a.kv_tiles) * a.max_seq + pos) * 128;
+                dst[p] = (int16_t)y0;
+                dst[p + half] = (int16_t)y1;
             }
         }
     }
@@ -262,6 +285,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
     const int S = a.stages;
     char *bsl = ring + (size_t)S * kMmaItemBytes;
     int32_t *ys = reinterpret_cast<int32_t *>(bsl + (size_t)a.max_items * 2048);  // [8][128]
+    int16_t *etab_s = reinterpret_cast<int16_t *>(ys + kMaxRows * 128);            // [2049] SiLU exp table
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int items = a.T * a.C;
     const int w0 = first_item(blockIdx.x, items, gridDim.x), w1 = first_item(blockIdx.x + 1, items, gridDim.x);
@@ -322,6 +346,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
         pdl_wait();
         pdl_trigger();
         const Step st = *a.step;
+        if (EPI == EPI_SILU)
+            for (int i = tid; i < 2049; i += 160) etab_s[i] = a.etab[i];
         mma_stage_rows(a, bsl, w0, n, st.rows, tid, 160, inv_s, red);
         named_sync(1, 160);
 
@@ -395,24 +421,35 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
                     int64_t *slot = a.scratch + ((size_t)(blockIdx.x * 2 + which) * kMaxRows) * 128;
 #pragma unroll
                     for (int r = 0; r < kMaxRows; r++) slot[r * 128 + m] = Sm[r];
-                    __threadfence();
-                    named_sync(3, 128);
+                    named_sync(3, 128);  // every thread's slot writes happen before thread 0's release below
                     const int b_lo = cta_of_item(t * a.C, items, gridDim.x);
                     const int b_hi = cta_of_item((t + 1) * a.C - 1, items, gridDim.x);
-                    if (m == 0) *last_s = atomicAdd(a.tile_cnt + t, 1) == b_hi - b_lo;
+                    if (m == 0) {
+                        int old;
+                        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.tile_cnt + t) : "memory");
+                        *last_s = old == b_hi - b_lo;
+                    }
                     named_sync(3, 128);
                     if (!*last_s) continue;
-                    __threadfence();
-                    for (int bb = b_lo; bb <= b_hi; bb++) {
-                        if (bb == (int)blockIdx.x) continue;
-                        const int wh = t == first_item(bb, items, gridDim.x) / a.C ? 0 : 1;
-                        const int64_t *o = a.scratch + ((size_t)(bb * 2 + wh) * kMaxRows) * 128;
+                    for (int b0 = b_lo; b0 <= b_hi; b0 += 4) {  // 4 contributors' loads in flight
+                        int64_t part[4][kMaxRows];
 #pragma unroll
-                        for (int r = 0; r < kMaxRows; r++) Sm[r] += __ldcg(o + r * 128 + m);
+                        for (int k = 0; k < 4; k++) {
+                            const int bb = b0 + k;
+                            const bool use = bb <= b_hi && bb != (int)blockIdx.x;
+                            const int wh = use && t != first_item(bb, items, gridDim.x) / a.C ? 1 : 0;
+                            const int64_t *o = a.scratch + ((size_t)((use ? bb : 0) * 2 + wh) * kMaxRows) * 128;
+#pragma unroll
+                            for (int r = 0; r < kMaxRows; r++) part[k][r] = use ? __ldcg(o + r * 128 + m) : 0;
+                        }
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+#pragma unroll
+                            for (int r = 0; r < kMaxRows; r++) Sm[r] += part[k][r];
                     }
                     if (m == 0) a.tile_cnt[t] = 0;  // ready for the next launch
                 }
-                mma_epilogue<EPI>(a, st, t, m, Sm, ys);
+                mma_epilogue<EPI>(a, st, t, m, Sm, ys, etab_s);
             }
         }
     }
@@ -426,7 +463,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
 }
 
 size_t mma_smem_bytes(int stages, int max_items) {
-    return kMmaHdr + (size_t)stages * kMmaItemBytes + (size_t)max_items * 2048 + (size_t)kMaxRows * 128 * 4;
+    return kMmaHdr + (size_t)stages * kMmaItemBytes + (size_t)max_items * 2048 + (size_t)kMaxRows * 128 * 4 + 4224;
 }
 
 // Ring depth that fits shared memory (2..kMaxStages stages).

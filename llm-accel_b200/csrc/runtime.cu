@@ -116,6 +116,11 @@ struct llmx_ctx {
     // scratch and tile counters (LLMX_MMA=0 disables, LLMX_MMA_MIN_ROWS)
     bool mma = false;
     int mma_min_rows = 3;
+    // projections on the tensor cores: bits MP_QKV, MP_O, MP_GU, MP_D (LLMX_MMA_PROJ).
+    // Default Gate/Up + Down: measured on B200 at 8 rows, Gate/Up 34.6 vs 39.0 us and
+    // Down 21.1 vs 31.0 us on the tensor cores, while QKV (11.2 vs 10.0) and O (12.0
+    // vs 5.9) are latency bound and stay on the dp2a kernel
+    int mma_proj = 0xC;
     MmaGeom mg[4]{};             // QKV, O, Gate/Up, Down of this rank
     size_t mma_layer_bytes = 0;
     uint8_t *mbuf = nullptr;
@@ -311,7 +316,9 @@ ProjArgs down_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in)
 
 enum { MP_QKV = 0, MP_O = 1, MP_GU = 2, MP_D = 3 };
 
-bool use_mma(const llmx_ctx *c, uint32_t rows) { return c->mma && (int)rows >= c->mma_min_rows; }
+bool use_mma(const llmx_ctx *c, uint32_t rows, int proj) {
+    return c->mma && (int)rows >= c->mma_min_rows && ((c->mma_proj >> proj) & 1);
+}
 
 // A peer all-reduce whose finishing step is still to come: its number within
 // the call, the residual to add and where the finished rows belong.
@@ -338,7 +345,7 @@ void take_input(llmx_ctx *c, ProjArgs &a, PendingAr &pend) {
 int after_partial(llmx_ctx *c, uint32_t rows, uint32_t &ar_next, int16_t *out, const int16_t *resid, bool fuse,
                   PendingAr &pend) {
     const uint32_t off = ar_next++;
-    if (fuse && c->ar.n > 1 && (int)rows <= c->ar_fuse_rows && !use_mma(c, rows)) {
+    if (fuse && c->ar.n > 1 && (int)rows <= c->ar_fuse_rows && !use_mma(c, rows, MP_QKV) && !use_mma(c, rows, MP_GU)) {
         pend.active = true;
         pend.off = off;
         pend.resid = resid;
@@ -404,7 +411,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         ProjArgs a = qkv_args(c, layer, in);
         take_input(c, a, pend);
-        if (use_mma(c, rows)) {
+        if (use_mma(c, rows, MP_QKV)) {
             const int rc = launch_mma(c, a, MP_QKV, layer, EPI_QKV);
             if (rc) return rc;
         } else {
@@ -417,7 +424,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         CK(launch_attn(t, (int)rows, c->stream));
         ProjArgs o = o_args(c, layer, out, in);
         o.ar_off = ar_next;
-        if (use_mma(c, rows)) {
+        if (use_mma(c, rows, MP_O)) {
             const int rc = launch_mma(c, o, MP_O, layer, ge);
             if (rc) return rc;
         } else {
@@ -433,14 +440,18 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         take_input(c, g, pend);
         ProjArgs d = down_args(c, layer, out, in);
         d.ar_off = ar_next;
-        if (use_mma(c, rows)) {
-            int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
-            if (!rc) rc = launch_mma(c, d, MP_D, layer, ge);
+        if (use_mma(c, rows, MP_GU)) {
+            const int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
+            if (rc) return rc;
+        } else {
+            set_stages(c, g, EPI_SILU, rt);
+            CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
+        }
+        if (use_mma(c, rows, MP_D)) {
+            const int rc = launch_mma(c, d, MP_D, layer, ge);
             if (rc) return rc;
             c->launches += 2;
         } else if (rt == 8 && c->size == 1) {
-            set_stages(c, g, EPI_SILU, rt);
-            CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
             // an 8-row block as two 4-row launches: 8 FFN-wide activation rows would
             // fill shared memory and starve the weight ring; 4 rows leave it room
             for (int half = 0; half < 2; half++) {
@@ -454,8 +465,6 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
             }
             c->launches += 3;
         } else {
-            set_stages(c, g, EPI_SILU, rt);
-            CK(launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream));
             set_stages(c, d, ge, rt);
             CK(launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream));
             c->launches += 2;
@@ -736,6 +745,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     // tensor-core projections for blocks of mma_min_rows..8 rows: QKV tiles are
     // heads, so head_dim must be 128 (every Qwen profile); LLMX_MMA=0 disables
     c->mma_min_rows = env_int("LLMX_MMA_MIN_ROWS", 3, 1, 9);
+    c->mma_proj = env_int("LLMX_MMA_PROJ", 0xC, 0, 0xF);
     if (hd == 128 && env_int("LLMX_MMA", 1, 0, 1) == 1) {
         auto cdiv = [](int a, int b) { return (a + b - 1) / b; };
         MmaGeom *g = c->mg;
@@ -1054,7 +1064,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         switch (kernel) {
         case LLMX_KERNEL_QKV: {
             ProjArgs a = qkv_args(c, layer, in);
-            if (use_mma(c, rows)) return launch_mma(c, a, MP_QKV, layer, EPI_QKV) ? cudaErrorUnknown : cudaSuccess;
+            if (use_mma(c, rows, MP_QKV)) return launch_mma(c, a, MP_QKV, layer, EPI_QKV) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
@@ -1067,20 +1077,20 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
             o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
-            if (use_mma(c, rows)) return launch_mma(c, o, MP_O, layer, ge) ? cudaErrorUnknown : cudaSuccess;
+            if (use_mma(c, rows, MP_O)) return launch_mma(c, o, MP_O, layer, ge) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, o, ge, rt);
             return launch_proj(o, ge, rt, grid_for(c, o.npairs, rt, o.K), c->stream);
         }
         case LLMX_KERNEL_GATE_UP: {
             ProjArgs g = gu_args(c, layer, in);
-            if (use_mma(c, rows)) return launch_mma(c, g, MP_GU, layer, EPI_SILU) ? cudaErrorUnknown : cudaSuccess;
+            if (use_mma(c, rows, MP_GU)) return launch_mma(c, g, MP_GU, layer, EPI_SILU) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, g, EPI_SILU, rt);
             return launch_proj(g, EPI_SILU, rt, grid_for(c, g.npairs, rt, g.K), c->stream);
         }
         case LLMX_KERNEL_DOWN: {
             ProjArgs d = down_args(c, layer, out, in);
             d.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
-            if (use_mma(c, rows)) return launch_mma(c, d, MP_D, layer, ge) ? cudaErrorUnknown : cudaSuccess;
+            if (use_mma(c, rows, MP_D)) return launch_mma(c, d, MP_D, layer, ge) ? cudaErrorUnknown : cudaSuccess;
             set_stages(c, d, ge, rt);
             return launch_proj(d, ge, rt, grid_for(c, d.npairs, rt, d.K), c->stream);
         }
