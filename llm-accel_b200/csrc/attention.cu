@@ -266,6 +266,249 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Blocks of several rows: one cluster per query head handles every row of the
+// block, so the K and V tiles of the head are read once for all rows.  Row r
+// sees positions < position + r + 1 (its own causal context); the cluster's
+// tiles cover the longest row.  Per row the arithmetic, the tile order and the
+// exchange are those of k_attn above.
+// ---------------------------------------------------------------------------
+struct AttnRowsSmem {
+    int16_t *kv;    // [tpc*64][kKvStride]  K rows, then V rows, shared by the rows
+    int16_t *ptab;  // [2049]
+    int16_t *q;     // [kMaxRows][hd]
+    int16_t *sc;    // [kMaxRows][tpc*64]  scores, then probabilities
+    int16_t *tvr;   // [kMaxRows][kMaxTiles][hd/C]
+    int32_t *mloc;  // [kMaxRows][kMaxTiles]
+    int32_t *gsum;  // [kMaxRows][kMaxTiles]
+    int32_t *gold;  // [kMaxRows][kMaxTiles]
+    int32_t *tsum;  // [kMaxRows][tpc]
+};
+
+static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[9]) {
+    const size_t P = (size_t)tpc * kTile;
+    size_t b = 0;
+    off[0] = b; b = align16(b + P * kKvStride * 2);
+    off[1] = b; b = align16(b + 2049 * 2);
+    off[2] = b; b = align16(b + (size_t)kMaxRows * kMaxHd * 2);
+    off[3] = b; b = align16(b + (size_t)kMaxRows * P * 2);
+    off[4] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * (kMaxHd / cl) * 2);
+    off[5] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
+    off[6] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
+    off[7] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
+    off[8] = b; b = align16(b + (size_t)kMaxRows * tpc * 4);
+    return b;
+}
+
+size_t attn_rows_smem_bytes(int tpc, int cluster) {
+    size_t off[9];
+    return attn_rows_layout(tpc, cluster, off);
+}
+
+constexpr int kAttnRowsThreads = 256;
+
+template <int C>
+__global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a) {
+    extern __shared__ __align__(16) char raw[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int c = (int)cluster.block_rank();
+    const int lh = blockIdx.x / C;
+    const int hd = a.hd, vpr = hd >> 3, epc = hd / C;
+    size_t off[9];
+    attn_rows_layout(a.tpc_max, C, off);
+    AttnRowsSmem m;
+    m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
+    m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
+    m.q = reinterpret_cast<int16_t *>(raw + off[2]);
+    m.sc = reinterpret_cast<int16_t *>(raw + off[3]);
+    m.tvr = reinterpret_cast<int16_t *>(raw + off[4]);
+    m.mloc = reinterpret_cast<int32_t *>(raw + off[5]);
+    m.gsum = reinterpret_cast<int32_t *>(raw + off[6]);
+    m.gold = reinterpret_cast<int32_t *>(raw + off[7]);
+    m.tsum = reinterpret_cast<int32_t *>(raw + off[8]);
+    const int P = a.tpc_max * kTile;  // row stride of sc
+
+    for (int i = threadIdx.x; i < 2049; i += blockDim.x) m.ptab[i] = a.ptab[i];
+    pdl_wait();
+    pdl_trigger();
+    const Step st = *a.step;
+    const int R = st.rows;
+    const int ntiles = (st.position + R + kTile - 1) / kTile;  // the longest row's tiles
+    const int tpc = max(1, (ntiles + C - 1) / C);
+    const int t_begin = min(c * tpc, ntiles), t_end = min(t_begin + tpc, ntiles);
+    const int nown = t_end - t_begin;
+    const int p_begin = t_begin * kTile;
+    const int npos = nown > 0 ? min(t_end * kTile, st.position + R) - p_begin : 0;
+    auto npos_of = [&](int r) { return max(0, min(npos, st.position + r + 1 - p_begin)); };
+    auto ntiles_of = [&](int r) { return (st.position + r + 1 + kTile - 1) / kTile; };
+    const int kvh = (a.first_head + lh) / a.gqa;
+    const int16_t *kb = a.kc + ((size_t)kvh * a.max_seq + p_begin) * hd;
+    const int16_t *vb = a.vc + ((size_t)kvh * a.max_seq + p_begin) * hd;
+
+    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
+        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
+        cp_async16(m.kv + pp * kKvStride + cc, kb + (size_t)pp * hd + cc);
+    }
+    for (int i = threadIdx.x; i < R * vpr; i += blockDim.x) {
+        const int r = i / vpr, v = i - r * vpr;
+        reinterpret_cast<uint4 *>(m.q + r * kMaxHd)[v] =
+            reinterpret_cast<const uint4 *>(a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd)[v];
+    }
+    for (int i = threadIdx.x; i < R * tpc; i += blockDim.x) m.tsum[i] = 0;
+    cp_async_wait_all();
+    __syncthreads();
+
+    // ---- 1. scores of every (row, position) of the row's context -----------
+    for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
+        const int r = i / npos, pp = i - r * npos;
+        if (pp >= npos_of(r)) continue;
+        const uint4 *qv = reinterpret_cast<const uint4 *>(m.q + r * kMaxHd);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
+        int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        auto add8 = [&](int32_t (&cc)[4], const uint4 q, const uint4 k) {
+            cc[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
+            cc[1] += qk_prod(hi16(q.x), q412(hi16(k.x)));
+            cc[2] += qk_prod(lo16(q.y), q412(lo16(k.y)));
+            cc[3] += qk_prod(hi16(q.y), q412(hi16(k.y)));
+            cc[0] += qk_prod(lo16(q.z), q412(lo16(k.z)));
+            cc[1] += qk_prod(hi16(q.z), q412(hi16(k.z)));
+            cc[2] += qk_prod(lo16(q.w), q412(lo16(k.w)));
+            cc[3] += qk_prod(hi16(q.w), q412(hi16(k.w)));
+        };
+        int e8 = 0;
+        for (; e8 + 1 < vpr; e8 += 2) {
+            add8(b[0], qv[e8], kv[e8]);
+            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
+        }
+        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        int64_t t64 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
+        int32_t tot = sat32(t64);
+        tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));
+        m.sc[r * P + pp] = (int16_t)sat16(rnd(tot, 8));
+    }
+    __syncthreads();  // K consumed: the buffer now receives V
+    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
+        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
+        cp_async16(m.kv + pp * kKvStride + cc, vb + (size_t)pp * hd + cc);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    {   // tile maxima of every (row, owned tile in the row's context): one warp each
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int w = warp; w < R * nown; w += blockDim.x >> 5) {
+            const int r = w / nown, tl = w - r * nown;
+            const int pe = min(kTile, npos_of(r) - tl * kTile);
+            if (pe <= 0) continue;
+            int32_t mx = -32768;
+            for (int j = lane; j < pe; j += 32) mx = max(mx, (int32_t)m.sc[r * P + tl * kTile + j]);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane < C) *cluster.map_shared_rank(m.mloc + r * kMaxTiles + t_begin + tl, lane) = mx;
+        }
+    }
+    cluster.sync();
+
+    // ---- 2. probabilities, tile sums and rescale factors, PV ----------------
+    for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
+        const int r = i / npos, pp = i - r * npos;
+        if (pp >= npos_of(r)) continue;
+        const int t = t_begin + pp / kTile;
+        const int32_t *ml = m.mloc + r * kMaxTiles;
+        int32_t mt = -32768;
+        for (int u = 0; u <= t; u++) mt = max(mt, ml[u]);
+        int32_t d = sat16((int32_t)m.sc[r * P + pp] - mt);
+        d = d < -2048 ? -2048 : (d > 0 ? 0 : d);
+        const int32_t pr = m.ptab[d + 2048];
+        m.sc[r * P + pp] = (int16_t)pr;
+        atomicAdd(m.tsum + r * tpc + pp / kTile, pr * 4);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * nown; i += blockDim.x) {
+        const int r = i / nown, tl = i - r * nown, t = t_begin + tl;
+        if (t >= ntiles_of(r)) continue;
+        const int32_t *ml = m.mloc + r * kMaxTiles;
+        int32_t mprev = -32768;
+        for (int u = 0; u < t; u++) mprev = max(mprev, ml[u]);
+        const int32_t mt = max(mprev, ml[t]);
+        int32_t d = sat16(mprev - mt);
+        d = d < -2048 ? -2048 : d;
+        const int32_t old = m.ptab[d + 2048];
+        for (int k = 0; k < C; k++) {
+            *cluster.map_shared_rank(m.gsum + r * kMaxTiles + t, k) = m.tsum[r * tpc + tl];
+            *cluster.map_shared_rank(m.gold + r * kMaxTiles + t, k) = old;
+        }
+    }
+    for (int i = threadIdx.x; i < R * nown * hd; i += blockDim.x) {
+        const int r = i / (nown * hd), rem = i - r * nown * hd, tli = rem / hd, e = rem - tli * hd;
+        const int pb = tli * kTile, pe = min(pb + kTile, npos_of(r));
+        if (pe <= pb) continue;
+        const int16_t *scr = m.sc + r * P;
+        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+        int pp = pb;
+        for (; pp + 3 < pe; pp += 4) {
+            b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
+            b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+            b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+            b3 += qk_prod(scr[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
+        }
+        if (pp < pe) b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
+        if (pp + 1 < pe) b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+        if (pp + 2 < pe) b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+        int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
+        ts = sat32(rnd((int64_t)ts * 1024, 16));
+        const int16_t tv = (int16_t)sat16(rnd(ts, 8));
+        *cluster.map_shared_rank(m.tvr + (r * kMaxTiles + t_begin + tli) * epc + e / C, e % C) = tv;
+    }
+    cluster.sync();
+
+    // ---- 3. in-order Q16.16 recurrence per row ------------------------------
+    for (int i = threadIdx.x; i < R * epc; i += blockDim.x) {
+        const int r = i / epc, j = i - r * epc, e = j * C + c;
+        const int nt = ntiles_of(r);
+        int32_t sum = 0, acc = 0;
+        for (int u = 0; u < nt; u++) {
+            const int64_t o = (int64_t)m.gold[r * kMaxTiles + u] * 4;
+            sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[r * kMaxTiles + u]);
+            acc = sat32(rnd((int64_t)acc * o, 16));
+            acc = sat32((int64_t)acc + (int64_t)m.tvr[(r * kMaxTiles + u) * epc + j] * 256);
+        }
+        const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
+        a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
+    }
+}
+
+cudaError_t attn_rows_configure(int max_smem_bytes, int cluster) {
+    if (cluster == kClusterWide) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_rows<kClusterWide>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        return cudaFuncSetAttribute(k_attn_rows<kClusterWide>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+    }
+    return cudaFuncSetAttribute(k_attn_rows<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+}
+
+cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
+    AttnArgs c = a;
+    void *args[] = {&c};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.cluster * a.q_heads, 1);
+    cfg.blockDim = dim3(kAttnRowsThreads);
+    cfg.dynamicSmemBytes = attn_rows_smem_bytes(a.tpc_max, a.cluster);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn_rows<kClusterWide> : (const void *)k_attn_rows<kCluster>;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 cudaError_t attn_configure(int max_smem_bytes, int cluster) {
     if (cluster == kClusterWide) {
         cudaError_t e = cudaFuncSetAttribute(k_attn<kClusterWide>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);

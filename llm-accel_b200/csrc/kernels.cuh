@@ -196,6 +196,10 @@ cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s);
 cudaError_t attn_configure(int max_smem_bytes, int cluster);
+// Blocks of several rows: one cluster per query head for all rows (K/V read once).
+cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s);
+cudaError_t attn_rows_configure(int max_smem_bytes, int cluster);
+size_t attn_rows_smem_bytes(int tpc, int cluster);
 size_t attn_smem_bytes(int tpc, int hd, int cluster);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);

@@ -78,6 +78,8 @@ struct llmx_ctx {
     // 256 CTAs, oversubscribe the SMs and stay on 8-CTA clusters)
     int tpc_max_wide = 0;
     bool attn_wide = false;
+    int attn_rows_min = 2;
+    bool attn_rows_wide = false;  // all-rows kernel on 16-CTA clusters (LLMX_ATTN_ROWS_WIDE)  // blocks of at least this many rows use the all-rows attention kernel (LLMX_ATTN_ROWS_MIN)
     int attn_wide_div = 1;  // wide clusters while rows x heads x 16 CTAs <= SMs / div (LLMX_ATTN_WIDE_DIV)
     // weights: per layer [QKV | O | GU | D] words
     size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
@@ -259,12 +261,30 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     return t;
 }
 
+// Attention of a block: the per-(row, head) kernel, or for blocks of at least
+// attn_rows_min rows one cluster per head covering every row.
+cudaError_t launch_attention(llmx_ctx *c, AttnArgs t, uint32_t rows);
+
 // Cluster size of an attention launch of `rows` rows.
 void pick_attn_cluster(const llmx_ctx *c, AttnArgs &t, uint32_t rows) {
     if (c->attn_wide && c->attn_wide_div * (int)rows * c->hq * kClusterWide <= c->nsm) {
         t.cluster = kClusterWide;
         t.tpc_max = c->tpc_max_wide;
     }
+}
+
+cudaError_t launch_attention(llmx_ctx *c, AttnArgs t, uint32_t rows) {
+    if ((int)rows >= c->attn_rows_min) {
+        t.pf_per_tile = 0;
+        if (c->attn_rows_wide) {  // 16 CTAs per head: the block's rows multiply each CTA's work
+            t.cluster = kClusterWide;
+            t.tpc_max = c->tpc_max_wide;
+        }
+        return launch_attn_rows(t, c->stream);
+    }
+    pick_attn_cluster(c, t, rows);
+    if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
+    return launch_attn(t, (int)rows, c->stream);
 }
 
 ProjArgs o_args(llmx_ctx *c, uint32_t layer, int16_t *out, const int16_t *in) {
@@ -418,10 +438,7 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
             set_stages(c, a, EPI_QKV, rt);
             CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         }
-        AttnArgs t = attn_args(c, layer);
-        pick_attn_cluster(c, t, rows);
-        if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
-        CK(launch_attn(t, (int)rows, c->stream));
+        CK(launch_attention(c, attn_args(c, layer), rows));
         ProjArgs o = o_args(c, layer, out, in);
         o.ar_off = ar_next;
         if (use_mma(c, rows, MP_O)) {
@@ -711,12 +728,21 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     e = proj_configure(kProjSmem);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
     e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster), kCluster);
+    if (e == cudaSuccess) e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
+    c->attn_rows_min = env_int("LLMX_ATTN_ROWS_MIN", 2, 2, 9);
+    if (hd % kClusterWide == 0 && env_int("LLMX_ATTN_ROWS_WIDE", 0, 0, 1) == 1) {
+        e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max_wide, kClusterWide), kClusterWide);
+        if (e == cudaSuccess) c->attn_rows_wide = true;
+        else (void)cudaGetLastError();
+    }
     // LLMX_ATTN_WIDE=0 keeps 8-CTA clusters everywhere
     c->attn_wide_div = env_int("LLMX_ATTN_WIDE_DIV", 1, 1, 8);
     if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && c->attn_wide_div * c->hq * kClusterWide <= c->nsm &&
         env_int("LLMX_ATTN_WIDE", 1, 0, 1) == 1) {
         e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide), kClusterWide);
+        if (e == cudaSuccess)
+            e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max_wide, kClusterWide), kClusterWide);
         if (e == cudaSuccess) c->attn_wide = true;
         else (void)cudaGetLastError();  // keep 8-CTA clusters
     }
@@ -1068,12 +1094,7 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
             set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
-        case LLMX_KERNEL_ATTN: {
-            AttnArgs t = attn_args(c, layer);
-            pick_attn_cluster(c, t, rows);
-            if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
-            return launch_attn(t, (int)rows, c->stream);
-        }
+        case LLMX_KERNEL_ATTN: return launch_attention(c, attn_args(c, layer), rows);
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
             o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank

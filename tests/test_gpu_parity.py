@@ -234,3 +234,30 @@ def test_prefill_sweep_device_built_cache(llmx, oracle):
     finally:
         oracle.set_threads(1)
         acc.close()
+
+
+@pytest.mark.parametrize("env", [{"LLMX_MMA_PROJ": "15"}, {"LLMX_MMA": "0"}], ids=["all_tensor_core", "all_dp2a"])
+@pytest.mark.parametrize("rows", [3, 8])
+def test_projection_kernels_both_paths(llmx, oracle, monkeypatch, env, rows):
+    """Blocks of 3..8 rows run Gate/Up and Down on the tensor cores by default
+    (byte-split int8 tcgen05.mma) and QKV / O on the dp2a kernel; every
+    projection has both kernels.  Force each choice for all four projections
+    (LLMX_MMA_PROJ=15: all on the tensor cores; LLMX_MMA=0: all dp2a) and match
+    the oracle on a Gaussian layer, a block at a tile edge and a decode row."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    s = llmx.shape("qwen-layer-long")
+    m = llmx.Model(s).init_gaussian(20260718 + rows, 0.02)
+    acc = llmx.Accelerator(s)
+    acc.upload_model(m)
+    ref = OracleState(oracle, oracle_shape(oracle, s), [m.layer(0)], m.norms())
+    rng = np.random.default_rng(rows)
+    k, v = random_kv(rng, s.kv_heads, 61, s.head_dim)
+    acc.write_kv(0, 0, k, v)
+    ref.kc[0][:, :61] = k
+    ref.vc[0][:, :61] = v
+    h = m.embed(rng.integers(0, s.vocab, rows))
+    _assert_same(acc.stack(h, position=61), ref.stack(h, 61), f"{rows}-row block")
+    d = m.embed([int(rng.integers(0, s.vocab))])
+    _assert_same(acc.stack(d, position=61 + rows), ref.stack(d, 61 + rows), "decode")
+    acc.close()
