@@ -435,10 +435,11 @@ size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_
 // Down rows) fills a stage alone and would leave one warp per stage to digest
 // it, so such units are split over P = 4 (or, for a deeper ring, 2) warps.  Limits: G*B*P <= consumer
 // warps of the kernel, G >= 2 (double buffering), shared memory within max_smem.
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts) {
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts,
+                int max_warps) {
     const int U = (epi == EPI_QKV || epi == EPI_SILU) ? 2 : 1;
     const int unit = U * K * 2;
-    const int cmax = 16;
+    const int cmax = max_warps < 2 ? 2 : (max_warps > 16 ? 16 : max_warps);  // consumer warps
     int B = (32 * 1024) / unit;
     if (B < 1) B = 1;
     if (B > cmax / 2) B = cmax / 2;

@@ -205,7 +205,8 @@ cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 cudaError_t proj_configure(int max_smem_bytes);
 size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk, int parts);
-int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts);
+int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts,
+                int max_warps);
 
 // Weight layout kernel (model upload): slot s of the destination receives
 // dense row row_of_slot[s], columns [col0, col0+K), as K/2 32-bit words; word j

@@ -94,6 +94,7 @@ struct llmx_ctx {
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
+    int gemv_warps = 16;  // consumer warps of a projection CTA at most (LLMX_GEMV_WARPS)
     // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_tile_kb
     // KiB per 64-position context tile from the layer's O weights on, at most
     // attn_pf_kb KiB and the end of Gate/Up (LLMX_ATTN_PREFETCH_TILE_KB, _KB, _ROWS).
@@ -184,7 +185,7 @@ void set_stages(llmx_ctx *c, ProjArgs &a, int epi, int rt) {
     const int smem = kProjSmem / c->gemv_ctas_per_sm - 1024;
     // FFN-wide inputs (the Down projection) may take their own ring size
     const int ring = a.K > 4 * c->s.hidden ? c->ring_wide_kb : (epi == EPI_SILU ? c->ring_gu_kb : c->ring_kb);
-    a.stages = gemv_stages(rt, epi, a.K, smem, ring * 1024, &a.units_per_chunk, &a.parts);
+    a.stages = gemv_stages(rt, epi, a.K, smem, ring * 1024, &a.units_per_chunk, &a.parts, c->gemv_warps);
     a.error = c->err;
 }
 
@@ -712,6 +713,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
+    c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
     auto bail = [&](int code) {
         release(c);

@@ -7,7 +7,10 @@ weights), preloads a seeded KV cache to `--position`, then
   --eager : runs `--steps` eager Task 18/19/20 sequences (no CUDA graph) so that a
             profiler sees plain launches (ncu -k regex:... -c ...);
   --argmax: runs `--steps` device LM-head argmaxes over a 151,936 x 2048 table
-            (k_lm_scan + k_lm_pick) and prints their mean device time.
+            (k_lm_scan + k_lm_pick) and prints their mean device time;
+  --generate: greedy generation on the device (llmx_generate: k_embed_rows,
+            the stack, k_lm_scan + k_lm_pick) over `--layers` layers, 8 prompt
+            tokens and `--steps` new tokens.
 Usage: python llm-accel_b200/profile_case.py --layers 4 --position 512 --table
 """
 from __future__ import annotations
@@ -36,6 +39,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--argmax", action="store_true")
+    ap.add_argument("--generate", action="store_true")
     ap.add_argument("--kv-scale", type=float, default=600.0, help="std of the preloaded KV cache (raw Q8.8)")
     ap.add_argument("--hidden", type=int, default=0, help="override the shape (e.g. a tensor-parallel rank's heads)")
     ap.add_argument("--heads", type=int, default=0)
@@ -44,6 +48,8 @@ def main():
     args = ap.parse_args()
     if args.argmax:
         return argmax_case(args.steps)
+    if args.generate:
+        return generate_case(args.layers, args.steps)
     over = {k: v for k, v in (("hidden", args.hidden), ("heads", args.heads), ("kv_heads", args.kv_heads),
                               ("inter", args.inter)) if v}
     s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq, **over)
@@ -73,6 +79,17 @@ def main():
             acc.bind(0, 1)
             acc.task(llmx.OP_FINAL_NORM, 0, pos, args.rows)
         print("eager steps done")
+    acc.close()
+
+
+def generate_case(layers, steps):
+    s = llmx.shape("qwen2.5-3b", layers=layers, max_seq=64)
+    m = llmx.Model(s).init_gaussian(20260718, 0.02)
+    acc = llmx.Accelerator(s)
+    acc.upload_model(m)
+    acc.upload_vocab(m)
+    toks = acc.generate(list(range(100, 108)), steps)
+    print(json.dumps({"generated": toks}))
     acc.close()
 
 
