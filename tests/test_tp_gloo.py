@@ -77,7 +77,27 @@ def _tp_task19(O, s, W, norm, hidden, rank, world, all_reduce):
     return O.residual(hidden, O.round_partial(all_reduce(part)))
 
 
-def _worker(rank, world, port, profile):
+def _word_all_reduce(dist, torch, p, number):
+    """The device's peer all-reduce as a host model: each rank's exact partial
+    sums travel as 64-bit words {sum << 16 | tag} (the sum must fit 48 bits),
+    every rank receives every rank's words, checks the tag of all-reduce
+    `number` ((number mod 65535) + 1) and adds the sign-extended sums."""
+    p = np.ascontiguousarray(p, dtype=np.int64)
+    assert np.abs(p).max(initial=0) < (1 << 47), "partial sum does not fit the 48-bit word"
+    tag = number % 65535 + 1
+    words = (p.astype(np.uint64) << np.uint64(16)) | np.uint64(tag)
+    t = torch.from_numpy(words.view(np.int64).copy())
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    total = np.zeros_like(p)
+    for o in out:
+        w = o.numpy().view(np.uint64)
+        assert np.all((w & np.uint64(0xFFFF)) == np.uint64(tag)), "stale or foreign word"
+        total += w.view(np.int64) >> 16
+    return total
+
+
+def _worker(rank, world, port, profile, words=False):
     sys.path.insert(0, os.path.join(os.path.dirname(HERE), "oracle"))
     import torch
     import torch.distributed as dist
@@ -88,7 +108,12 @@ def _worker(rank, world, port, profile):
         O.build()
         O.set_exp_mode(O.EXP_TRUNC)
 
+        count = [0]
+
         def all_reduce(p):
+            if words:
+                count[0] += 1
+                return _word_all_reduce(dist, torch, p, count[0] - 1)
             t = torch.from_numpy(np.ascontiguousarray(p, dtype=np.int64))
             dist.all_reduce(t, op=dist.ReduceOp.SUM)
             return t.numpy()
@@ -119,7 +144,43 @@ def _worker(rank, world, port, profile):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("words", [False, True], ids=["sum", "tagged_words"])
 @pytest.mark.parametrize("profile", ["medium", "small"])
-def test_tensor_parallel_two_gloo_ranks(profile):
+def test_tensor_parallel_two_gloo_ranks(profile, words):
     mp = pytest.importorskip("torch.multiprocessing")
-    mp.spawn(_worker, args=(2, _free_port(), profile), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), profile, words), nprocs=2, join=True)
+
+
+def _leave_worker(rank, world, port, result_dir):
+    """Rank 1 leaves between steps (after the first all-reduce, nothing in
+    flight); rank 0's next all-reduce must end with an error within the
+    process group's short timeout instead of waiting for good."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    t = torch.ones(4, dtype=torch.int64)
+    dist.all_reduce(t)
+    msg = "ok" if int(t[0]) == world else "first step wrong"
+    if rank == 1:
+        dist.destroy_process_group()  # leaves the group between steps
+    else:
+        import time
+        t0 = time.time()
+        try:
+            dist.all_reduce(t)
+            msg = "the survivor's collective returned although its peer left"
+        except Exception:  # noqa: BLE001 -- any error is the detection we want
+            if time.time() - t0 > 60:
+                msg = "detected, but only after the timeout bound"
+    with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(msg)
+
+
+def test_rank_leaving_between_steps_is_detected(tmp_path):
+    mp = pytest.importorskip("torch.multiprocessing")
+    mp.spawn(_leave_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert (tmp_path / f"rank{r}.txt").read_text() == "ok", f"rank {r}"
