@@ -52,67 +52,6 @@ static __device__ __forceinline__ void cp_async_wait_all() {
 
 constexpr int kMaxTiles = kCluster * kMaxTilesPerCta;
 
-// ---- exact fast forms of the per-product rounding ---------------------------
-// qk_prod(x, q412(y)) = (x * sat16(16 y) + 8) >> 4 is exactly x * y for
-// -2048 <= y <= 2047 (16 y is a multiple of 16 and in range) and x * -2048 for
-// y < -2048; only y >= 2048 (sat16(16 y) = 32767) differs from
-// x * clamp(y, -2048, 2047).  The kernels clamp K and V to [-2048, 2047] in
-// shared memory and form plain integer products -- QK on the dp2a pipe with the
-// query split into bytes, PV as 32-bit multiply-adds -- and route every
-// position (QK) or tile (PV) that held a y >= 2048, and every query holding
-// -32768, through the per-product form again (rare in practice; exact always).
-// Without those, no product reaches 2^26 in magnitude, so no bank of <= 32
-// products saturates and the sum over all banks equals the banked sum.
-
-// Clamps the 8 int16 of v to [-2048, 2047]; true if one of them was >= 2048.
-static __device__ __forceinline__ bool clamp_k12(uint4 &v) {
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t sat = 0;
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-        sat |= __vcmpges2(w[q], 0x08000800u);
-        w[q] = __vmaxs2(__vmins2(w[q], 0x07FF07FFu), 0xF800F800u);
-    }
-    v = make_uint4(w[0], w[1], w[2], w[3]);
-    return sat != 0;
-}
-// A packed pair of query elements as dp2a operand bytes {lo q0, lo q1, hi q0, hi q1}.
-static __device__ __forceinline__ uint32_t q_pair_bytes(uint32_t w) { return __byte_perm(w, 0, 0x3120); }
-// QK of one position from clamped K (int16 pairs) and query bytes: exact sum of q * k.
-static __device__ __forceinline__ int32_t qk_dot_fast(const uint4 *__restrict__ k, const uint4 *__restrict__ qb,
-                                                      int vpr) {
-    int lo = 0, hi = 0;
-    for (int v = 0; v < vpr; v++) {
-        const uint4 kv = k[v], b = qb[v];
-        lo = dp2a_lo_su(kv.x, b.x, lo);
-        hi = dp2a_hi_ss(kv.x, b.x, hi);
-        lo = dp2a_lo_su(kv.y, b.y, lo);
-        hi = dp2a_hi_ss(kv.y, b.y, hi);
-        lo = dp2a_lo_su(kv.z, b.z, lo);
-        hi = dp2a_hi_ss(kv.z, b.z, hi);
-        lo = dp2a_lo_su(kv.w, b.w, lo);
-        hi = dp2a_hi_ss(kv.w, b.w, hi);
-    }
-    return sat32((int64_t)lo + 256 * (int64_t)hi);
-}
-// QK of one position by the per-product rounding, four saturating banks (k mod 4)
-// (golden_attention_mm host:3231-3276), from the unclamped rows in global memory.
-static __device__ int32_t qk_dot_exact(const int16_t *__restrict__ q, const int16_t *__restrict__ k, int hd) {
-    int64_t bank[4] = {0, 0, 0, 0};  // <= 32 products each: the saturating sum is sat32 of the exact one
-    for (int i = 0; i < hd; i++) bank[i & 3] += qk_prod(q[i], q412(k[i]));
-    int64_t t = 0;
-#pragma unroll
-    for (int j = 0; j < 4; j++) t += sat32(bank[j]);
-    return sat32(t);
-}
-// Raw-payload PV of one element over positions [0, n) by the per-product rounding,
-// from the unclamped V rows in global memory (banks never saturate).
-static __device__ int32_t pv_exact(const int16_t *__restrict__ p, const int16_t *__restrict__ v, int hd, int n) {
-    int64_t s = 0;
-    for (int pp = 0; pp < n; pp++) s += qk_prod(p[pp], q412(v[(size_t)pp * hd]));
-    return sat32(s);
-}
-
 struct AttnSmem {      // carved out of dynamic shared memory
     int16_t *kv;       // [tpc*64][kKvStride] raw Q8.8 K rows, then V rows, of the owned tiles
     int16_t *ptab;     // [2049] softmax exp table
@@ -123,14 +62,11 @@ struct AttnSmem {      // carved out of dynamic shared memory
     int32_t *gsum;     // [kMaxTiles] every tile's sum (pushed)
     int32_t *gold;     // [kMaxTiles] every tile's rescale factor (pushed)
     int32_t *tsum;     // [tpc] owned tile sums (local accumulation)
-    uint32_t *qb;      // [hd/2] query pairs as dp2a bytes
-    uint8_t *ksat;     // [tpc*64] position holds a k >= 2048 (exact path)
-    int32_t *vsat;     // [tpc] owned tile holds a v >= 2048 (exact path); [tpc] = query holds -32768
 };
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[12]) {
+static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[9]) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
     off[0] = b; b = align16(b + rows * kKvStride * 2);                       // kv
@@ -142,15 +78,12 @@ static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t of
     off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
     off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
     off[8] = b; b = align16(b + (size_t)tpc * 4);                            // tsum
-    off[9] = b; b = align16(b + (size_t)kMaxHd * 2);                         // qb
-    off[10] = b; b = align16(b + rows);                                      // ksat
-    off[11] = b; b = align16(b + (size_t)(tpc + 1) * 4);                     // vsat + query flag
     (void)hd;
     return b;
 }
 
 size_t attn_smem_bytes(int tpc, int hd, int cluster) {
-    size_t off[12];
+    size_t off[9];
     return attn_layout(tpc, hd, cluster, off);
 }
 
@@ -163,12 +96,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int lh = blockIdx.x / C;  // local query head
     const int r = blockIdx.y;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;  // elements finalised per CTA
-    size_t off[12];
+    size_t off[9];
     attn_layout(a.tpc_max, hd, C, off);
     AttnSmem m;
-    m.qb = reinterpret_cast<uint32_t *>(raw + off[9]);
-    m.ksat = reinterpret_cast<uint8_t *>(raw + off[10]);
-    m.vsat = reinterpret_cast<int32_t *>(raw + off[11]);
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
     m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
     m.q = reinterpret_cast<int16_t *>(raw + off[2]);
@@ -206,8 +136,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         for (int i = threadIdx.x; i < vpr; i += blockDim.x) reinterpret_cast<uint4 *>(m.q)[i] = qsrc[i];
     }
     for (int i = threadIdx.x; i < nown; i += blockDim.x) m.tsum[i] = 0;
-    for (int i = threadIdx.x; i < npos; i += blockDim.x) m.ksat[i] = 0;
-    for (int i = threadIdx.x; i <= tpc; i += blockDim.x) m.vsat[i] = 0;
     // L2 warm-up: the same byte count in every CTA (from the step record), one slice each
     const unsigned long long pf_n =
         min(a.pf_bytes, a.pf_per_tile * (unsigned long long)((st.position + st.rows + kTile - 1) / kTile)) & ~15ull;
@@ -215,25 +143,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         l2_prefetch_slice(a.pf, pf_n, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     cp_async_wait_all();
     __syncthreads();
-    // clamp K in place (flagging positions with a k >= 2048); query -> dp2a bytes
-    const int16_t *qg = a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd;
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        uint4 *kp = reinterpret_cast<uint4 *>(m.kv + pp * kKvStride + cc);
-        uint4 kv = *kp;
-        if (clamp_k12(kv)) m.ksat[pp] = 1;
-        *kp = kv;
-    }
-    for (int i = threadIdx.x; npos > 0 && i < vpr; i += blockDim.x) {
-        const uint4 qv = reinterpret_cast<const uint4 *>(m.q)[i];
-        if ((__vcmpeq2(qv.x, 0x80008000u) | __vcmpeq2(qv.y, 0x80008000u) | __vcmpeq2(qv.z, 0x80008000u) |
-             __vcmpeq2(qv.w, 0x80008000u)) != 0)
-            m.vsat[tpc] = 1;
-        reinterpret_cast<uint4 *>(m.qb)[i] =
-            make_uint4(q_pair_bytes(qv.x), q_pair_bytes(qv.y), q_pair_bytes(qv.z), q_pair_bytes(qv.w));
-    }
-    __syncthreads();
-    const bool q_min = m.vsat[tpc] != 0;
 
     // ---- 1. scores; owned tile maxima pushed to every CTA of the cluster ----
     // Banks k mod 4 of golden_attention_mm saturate in k order; a bank holds <= 32
@@ -242,11 +151,33 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     // exact sum.  Each bank is therefore summed as two exact int32 halves (even /
     // odd 16-byte vectors, <= 16 products each), added in int64 and saturated once.
     for (int pp = threadIdx.x; pp < npos; pp += blockDim.x) {
-        int32_t tot = m.ksat[pp] || q_min ? qk_dot_exact(qg, kb + (size_t)pp * hd, hd)
-                                          : qk_dot_fast(reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride),
-                                                        reinterpret_cast<const uint4 *>(m.qb), vpr);
+        const uint4 *qv = reinterpret_cast<const uint4 *>(m.q);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
+        int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        auto add8 = [&](int32_t (&c)[4], const uint4 q, const uint4 k) {
+            c[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
+            c[1] += qk_prod(hi16(q.x), q412(hi16(k.x)));
+            c[2] += qk_prod(lo16(q.y), q412(lo16(k.y)));
+            c[3] += qk_prod(hi16(q.y), q412(hi16(k.y)));
+            c[0] += qk_prod(lo16(q.z), q412(lo16(k.z)));
+            c[1] += qk_prod(hi16(q.z), q412(hi16(k.z)));
+            c[2] += qk_prod(lo16(q.w), q412(lo16(k.w)));
+            c[3] += qk_prod(hi16(q.w), q412(hi16(k.w)));
+        };
+        int e8 = 0;
+#pragma unroll 2
+        for (; e8 + 1 < vpr; e8 += 2) {
+            add8(b[0], qv[e8], kv[e8]);
+            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
+        }
+        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        int64_t t64 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
+        int32_t tot = sat32(t64);
         tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));  // x accum(fm(1/sqrt(d)))
-        m.sc[pp] = (int16_t)sat16(rnd(tot, 8));
+        const int32_t sc = sat16(rnd(tot, 8));
+        m.sc[pp] = (int16_t)sc;
     }
     __syncthreads();  // K consumed: the buffer now receives V (overlaps the exchange below)
     for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
@@ -283,13 +214,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {  // clamp V in place, flag tiles with v >= 2048
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        uint4 *vp = reinterpret_cast<uint4 *>(m.kv + pp * kKvStride + cc);
-        uint4 vv = *vp;
-        if (clamp_k12(vv)) m.vsat[pp / kTile] = 1;
-        *vp = vv;
-    }
     for (int i = threadIdx.x; i < nown; i += blockDim.x) {  // tile sum + rescale factor -> every CTA
         const int t = t_begin + i;
         int32_t mprev = -32768, mt = -32768;
@@ -303,35 +227,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
             *cluster.map_shared_rank(m.gold + t, k) = old;
         }
     }
-    __syncthreads();  // V clamped and tiles flagged
     // raw payload p (read as Q8.8) x V (Q4.12, saturated), rounded per product,
-    // four banks in position order (|p*v| <= 2^29: banks never saturate, so
-    // their sum is one exact sum), x accum(fm(1/64)), -> fm; pushed to the CTA
-    // that finalises element e.  One pair of elements per item.
-    for (int i = threadIdx.x; i < nown * (hd >> 1); i += blockDim.x) {
-        const int tli = i / (hd >> 1), e = 2 * (i - tli * (hd >> 1));
+    // four banks in position order (|p*v| <= 2^29: banks never saturate),
+    // x accum(fm(1/64)), -> fm; pushed to the CTA that finalises element e
+    for (int i = threadIdx.x; i < nown * hd; i += blockDim.x) {
+        const int tli = i / hd, e = i - tli * hd;
         const int pb = tli * kTile, pe = min(pb + kTile, npos);
-        int32_t s2[2];
-        if (m.vsat[tli]) {
-            s2[0] = pv_exact(m.sc + pb, vb + (size_t)pb * hd + e, hd, pe - pb);
-            s2[1] = pv_exact(m.sc + pb, vb + (size_t)pb * hd + e + 1, hd, pe - pb);
-        } else {  // |p * v| <= 2^14 * 2^11: 64 products stay within int32
-            int32_t a0 = 0, a1 = 0;
-            for (int pp = pb; pp < pe; pp++) {
-                const int32_t pr = m.sc[pp];
-                const uint32_t w = *reinterpret_cast<const uint32_t *>(m.kv + pp * kKvStride + e);
-                a0 += pr * lo16(w);
-                a1 += pr * hi16(w);
-            }
-            s2[0] = a0;
-            s2[1] = a1;
+        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+        int pp = pb;
+        for (; pp + 3 < pe; pp += 4) {
+            b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
+            b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+            b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+            b3 += qk_prod(m.sc[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
         }
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int32_t ts = sat32(rnd((int64_t)s2[h] * 1024, 16));
-            const int16_t tv = (int16_t)sat16(rnd(ts, 8));
-            *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + (e + h) / C, (e + h) % C) = tv;
-        }
+        if (pp < pe) b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
+        if (pp + 1 < pe) b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+        if (pp + 2 < pe) b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+        int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
+        ts = sat32(rnd((int64_t)ts * 1024, 16));
+        const int16_t tv = (int16_t)sat16(rnd(ts, 8));
+        *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
     }
     cluster.sync();
 
@@ -367,12 +283,9 @@ struct AttnRowsSmem {
     int32_t *gsum;  // [kMaxRows][kMaxTiles]
     int32_t *gold;  // [kMaxRows][kMaxTiles]
     int32_t *tsum;  // [kMaxRows][tpc]
-    uint32_t *qb;   // [kMaxRows][hd/2] query pairs as dp2a bytes
-    uint8_t *ksat;  // [tpc*64] position holds a k >= 2048
-    int32_t *vsat;  // [tpc] tile holds a v >= 2048; [tpc + r] = query row r holds -32768
 };
 
-static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[12]) {
+static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[9]) {
     const size_t P = (size_t)tpc * kTile;
     size_t b = 0;
     off[0] = b; b = align16(b + P * kKvStride * 2);
@@ -384,14 +297,11 @@ static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[1
     off[6] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
     off[7] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
     off[8] = b; b = align16(b + (size_t)kMaxRows * tpc * 4);
-    off[9] = b; b = align16(b + (size_t)kMaxRows * kMaxHd * 2);
-    off[10] = b; b = align16(b + P);
-    off[11] = b; b = align16(b + (size_t)(tpc + kMaxRows) * 4);
     return b;
 }
 
 size_t attn_rows_smem_bytes(int tpc, int cluster) {
-    size_t off[12];
+    size_t off[9];
     return attn_rows_layout(tpc, cluster, off);
 }
 
@@ -404,12 +314,9 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     const int c = (int)cluster.block_rank();
     const int lh = blockIdx.x / C;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;
-    size_t off[12];
+    size_t off[9];
     attn_rows_layout(a.tpc_max, C, off);
     AttnRowsSmem m;
-    m.qb = reinterpret_cast<uint32_t *>(raw + off[9]);
-    m.ksat = reinterpret_cast<uint8_t *>(raw + off[10]);
-    m.vsat = reinterpret_cast<int32_t *>(raw + off[11]);
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
     m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
     m.q = reinterpret_cast<int16_t *>(raw + off[2]);
@@ -448,38 +355,36 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
             reinterpret_cast<const uint4 *>(a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd)[v];
     }
     for (int i = threadIdx.x; i < R * tpc; i += blockDim.x) m.tsum[i] = 0;
-    for (int i = threadIdx.x; i < npos; i += blockDim.x) m.ksat[i] = 0;
-    for (int i = threadIdx.x; i < tpc + kMaxRows; i += blockDim.x) m.vsat[i] = 0;
     cp_async_wait_all();
-    __syncthreads();
-    // clamp K in place (flagging positions with a k >= 2048); queries -> dp2a bytes
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        uint4 *kp = reinterpret_cast<uint4 *>(m.kv + pp * kKvStride + cc);
-        uint4 kv = *kp;
-        if (clamp_k12(kv)) m.ksat[pp] = 1;
-        *kp = kv;
-    }
-    for (int i = threadIdx.x; i < R * vpr; i += blockDim.x) {
-        const int r = i / vpr, v = i - r * vpr;
-        const uint4 qv = reinterpret_cast<const uint4 *>(m.q + r * kMaxHd)[v];
-        if ((__vcmpeq2(qv.x, 0x80008000u) | __vcmpeq2(qv.y, 0x80008000u) | __vcmpeq2(qv.z, 0x80008000u) |
-             __vcmpeq2(qv.w, 0x80008000u)) != 0)
-            m.vsat[tpc + r] = 1;
-        reinterpret_cast<uint4 *>(m.qb + r * (kMaxHd / 2))[v] =
-            make_uint4(q_pair_bytes(qv.x), q_pair_bytes(qv.y), q_pair_bytes(qv.z), q_pair_bytes(qv.w));
-    }
     __syncthreads();
 
     // ---- 1. scores of every (row, position) of the row's context -----------
     for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
         const int r = i / npos, pp = i - r * npos;
         if (pp >= npos_of(r)) continue;
-        const int16_t *qg = a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd;
-        int32_t tot = m.ksat[pp] || m.vsat[tpc + r]
-                          ? qk_dot_exact(qg, kb + (size_t)pp * hd, hd)
-                          : qk_dot_fast(reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride),
-                                        reinterpret_cast<const uint4 *>(m.qb + r * (kMaxHd / 2)), vpr);
+        const uint4 *qv = reinterpret_cast<const uint4 *>(m.q + r * kMaxHd);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
+        int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        auto add8 = [&](int32_t (&cc)[4], const uint4 q, const uint4 k) {
+            cc[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
+            cc[1] += qk_prod(hi16(q.x), q412(hi16(k.x)));
+            cc[2] += qk_prod(lo16(q.y), q412(lo16(k.y)));
+            cc[3] += qk_prod(hi16(q.y), q412(hi16(k.y)));
+            cc[0] += qk_prod(lo16(q.z), q412(lo16(k.z)));
+            cc[1] += qk_prod(hi16(q.z), q412(hi16(k.z)));
+            cc[2] += qk_prod(lo16(q.w), q412(lo16(k.w)));
+            cc[3] += qk_prod(hi16(q.w), q412(hi16(k.w)));
+        };
+        int e8 = 0;
+        for (; e8 + 1 < vpr; e8 += 2) {
+            add8(b[0], qv[e8], kv[e8]);
+            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
+        }
+        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        int64_t t64 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
+        int32_t tot = sat32(t64);
         tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));
         m.sc[r * P + pp] = (int16_t)sat16(rnd(tot, 8));
     }
@@ -507,10 +412,7 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     // ---- 2. probabilities, tile sums and rescale factors, PV ----------------
     for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
         const int r = i / npos, pp = i - r * npos;
-        if (pp >= npos_of(r)) {  // outside row r's context: probability 0 adds nothing to PV
-            m.sc[r * P + pp] = 0;
-            continue;
-        }
+        if (pp >= npos_of(r)) continue;
         const int t = t_begin + pp / kTile;
         const int32_t *ml = m.mloc + r * kMaxTiles;
         int32_t mt = -32768;
@@ -523,13 +425,6 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {  // clamp V in place, flag tiles with v >= 2048
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        uint4 *vp = reinterpret_cast<uint4 *>(m.kv + pp * kKvStride + cc);
-        uint4 vv = *vp;
-        if (clamp_k12(vv)) m.vsat[pp / kTile] = 1;
-        *vp = vv;
-    }
     for (int i = threadIdx.x; i < R * nown; i += blockDim.x) {
         const int r = i / nown, tl = i - r * nown, t = t_begin + tl;
         if (t >= ntiles_of(r)) continue;
@@ -545,43 +440,26 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
             *cluster.map_shared_rank(m.gold + r * kMaxTiles + t, k) = old;
         }
     }
-    __syncthreads();  // V clamped, tiles flagged, probabilities final
-    // PV: one (tile, element pair) per item, its V words read once for every row
-    for (int i = threadIdx.x; i < nown * (hd >> 1); i += blockDim.x) {
-        const int tli = i / (hd >> 1), e = 2 * (i - tli * (hd >> 1));
-        const int pb = tli * kTile, pe = min(pb + kTile, npos);
-        int32_t acc[kMaxRows][2];
-#pragma unroll
-        for (int r = 0; r < kMaxRows; r++) acc[r][0] = acc[r][1] = 0;
-        if (m.vsat[tli]) {
-            for (int r = 0; r < R; r++) {
-                const int n = max(0, min(pe, npos_of(r)) - pb);
-                acc[r][0] = pv_exact(m.sc + r * P + pb, vb + (size_t)pb * hd + e, hd, n);
-                acc[r][1] = pv_exact(m.sc + r * P + pb, vb + (size_t)pb * hd + e + 1, hd, n);
-            }
-        } else {
-            for (int pp = pb; pp < pe; pp++) {
-                const uint32_t w = *reinterpret_cast<const uint32_t *>(m.kv + pp * kKvStride + e);
-                const int32_t v0 = lo16(w), v1 = hi16(w);
-#pragma unroll
-                for (int r = 0; r < kMaxRows; r++)
-                    if (r < R) {
-                        const int32_t pr = m.sc[r * P + pp];
-                        acc[r][0] += pr * v0;
-                        acc[r][1] += pr * v1;
-                    }
-            }
+    for (int i = threadIdx.x; i < R * nown * hd; i += blockDim.x) {
+        const int r = i / (nown * hd), rem = i - r * nown * hd, tli = rem / hd, e = rem - tli * hd;
+        const int pb = tli * kTile, pe = min(pb + kTile, npos_of(r));
+        if (pe <= pb) continue;
+        const int16_t *scr = m.sc + r * P;
+        int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+        int pp = pb;
+        for (; pp + 3 < pe; pp += 4) {
+            b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
+            b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+            b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+            b3 += qk_prod(scr[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
         }
-#pragma unroll
-        for (int r = 0; r < kMaxRows; r++) {
-            if (r >= R || t_begin + tli >= ntiles_of(r)) continue;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int32_t ts = sat32(rnd((int64_t)acc[r][h] * 1024, 16));
-                const int16_t tv = (int16_t)sat16(rnd(ts, 8));
-                *cluster.map_shared_rank(m.tvr + (r * kMaxTiles + t_begin + tli) * epc + (e + h) / C, (e + h) % C) = tv;
-            }
-        }
+        if (pp < pe) b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
+        if (pp + 1 < pe) b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
+        if (pp + 2 < pe) b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+        int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
+        ts = sat32(rnd((int64_t)ts * 1024, 16));
+        const int16_t tv = (int16_t)sat16(rnd(ts, 8));
+        *cluster.map_shared_rank(m.tvr + (r * kMaxTiles + t_begin + tli) * epc + e / C, e % C) = tv;
     }
     cluster.sync();
 

@@ -261,3 +261,31 @@ def test_projection_kernels_both_paths(llmx, oracle, monkeypatch, env, rows):
     d = m.embed([int(rng.integers(0, s.vocab))])
     _assert_same(acc.stack(d, position=61 + rows), ref.stack(d, 61 + rows), "decode")
     acc.close()
+
+
+@pytest.mark.parametrize("rows", [1, 8])
+def test_attention_saturating_operands(llmx, oracle, rows):
+    """K and V caches over the whole int16 range (many |k|, |v| >= 8.0, i.e. raw
+    >= 2048, where the Q4.12 conversion saturates) and hidden rows at the int16
+    extremes (saturated queries, some exactly -32768): the per-product rounding
+    and the saturating banks of both attention kernels must agree with the
+    oracle, for one row and an 8-row block."""
+    s = llmx.shape("qwen-layer-long")
+    m = llmx.Model(s).init_reference_random(5)
+    acc = llmx.Accelerator(s)
+    acc.upload_model(m)
+    ref = OracleState(oracle, oracle_shape(oracle, s), [m.layer(0)], m.norms())
+    rng = np.random.default_rng(77)
+    P = 200
+    k = rng.integers(-32768, 32768, (s.kv_heads, P, s.head_dim)).astype(np.int16)
+    v = rng.integers(-32768, 32768, (s.kv_heads, P, s.head_dim)).astype(np.int16)
+    k[:, ::3] = np.clip(k[:, ::3] // 16, -2047, 2047)  # a third of the positions unsaturated
+    v[:, :64] = np.clip(v[:, :64] // 16, -2047, 2047)  # the first tile of V unsaturated
+    acc.write_kv(0, 0, k, v)
+    ref.kc[0][:, :P] = k
+    ref.vc[0][:, :P] = v
+    h = rng.choice(np.array([-32768, 32767, -30000, 31000], np.int16), (rows, s.hidden))
+    _assert_same(acc.stack(h, position=P), ref.stack(h, P), f"{rows} saturating rows")
+    d = rng.integers(-2000, 2000, (1, s.hidden)).astype(np.int16)
+    _assert_same(acc.stack(d, position=P + rows), ref.stack(d, P + rows), "decode after")
+    acc.close()
