@@ -44,9 +44,24 @@ extern "C" {
 #define LLMX_ERR_UNSUPPORTED 107
 #define LLMX_ERR_TIMEOUT 108     /* a kernel's bounded wait expired (device error flag) */
 
-/* ---- coarse operators: operator_kind_t host:69-91 / cc8_operator_t
- *      include/control_cache_8x64.hpp:252-277 (only the resident tasks) ---- */
+/* ---- operators: operator_kind_t host:69-91 / cc8_operator_t
+ *      include/control_cache_8x64.hpp:252-277 ---- */
 #define LLMX_OP_NOP 0
+/* per-operator (feature) modes, llmx_run_feature */
+#define LLMX_OP_Q_PROJECTION 1
+#define LLMX_OP_K_PROJECTION 2
+#define LLMX_OP_V_PROJECTION 3
+#define LLMX_OP_O_PROJECTION 4
+#define LLMX_OP_FFN_GATE 5
+#define LLMX_OP_FFN_UP 6
+#define LLMX_OP_FFN_DOWN 7
+#define LLMX_OP_RMSNORM 8
+#define LLMX_OP_SILU_MUL 9
+#define LLMX_OP_RESIDUAL_ADD 10
+/* 11-15 (QK, PV, softmax, flash, decode smoke tile diagnostics): not served */
+#define LLMX_OP_DECODER_LAYER 16      /* full layer = Task 18 then Task 19, llmx_task */
+#define LLMX_OP_ATTN_PREFILL_BLOCK 17 /* llmx_run_prefill_attention_block */
+/* coarse resident tasks, llmx_task / llmx_stack */
 #define LLMX_OP_ATTENTION_SUBLAYER 18 /* Task 18 */
 #define LLMX_OP_FFN_SUBLAYER 19       /* Task 19 */
 #define LLMX_OP_FINAL_NORM 20         /* Task 20 */
@@ -97,6 +112,17 @@ int llmx_shape_validate(const llmx_shape *shape);
  * record the controller would emit (counters included) and returns st->code. */
 int llmx_validate_task(const llmx_shape *shape, uint32_t op, uint32_t layer,
                        uint32_t position, uint32_t rows, llmx_status *st);
+/* The same for the controller image with the per-operator schedulers
+ * (kernel/control_cache_8x64.cpp:6496-7497): additionally accepts the feature
+ * operators 1-10 (no position check; counters of :7273-7497) and the prefill
+ * block attention 17 (:6496-6522, counters of check_prefill_block_attention_status
+ * host:5587-5604).  Ops 11-15 get LLMX_BAD_OPERATOR. */
+int llmx_validate_operator(const llmx_shape *shape, uint32_t op, uint32_t layer,
+                           uint32_t position, uint32_t rows, llmx_status *st);
+/* feature_input_dim / feature_output_dim / needs_rhs host:2015-2061 of a feature
+ * operator (1-10); LLMX_ERR_ARG for any other operator. */
+int llmx_feature_dims(const llmx_shape *shape, uint32_t op, uint32_t *in_dim,
+                      uint32_t *out_dim, int *needs_rhs);
 
 /* Human-readable name of a return code. */
 const char *llmx_strerror(int code);
@@ -184,11 +210,34 @@ int llmx_write_hidden(llmx_ctx *ctx, uint32_t pair, const int16_t *rows_host,
 int llmx_read_hidden(llmx_ctx *ctx, uint32_t pair, int16_t *rows_host, uint32_t rows);
 /* bind_controller_data_ports host:1846-1888 (output pair, input pair). */
 int llmx_bind(llmx_ctx *ctx, uint32_t out_pair, uint32_t in_pair);
-/* execute_bound_resident_task host:1890-2053: runs Task 18/19/20 (or NOP) on
- * the bound pairs, stream-ordered, waits for completion and returns the
- * status record.  Returns st->code (0 = OK). */
+/* execute_bound_resident_task host:1890-2053: runs Task 18/19/20, the
+ * compatibility full-layer Task 16 (run_decoder_layer host:1136-1176; the
+ * input pair is left unchanged) or NOP on the bound pairs, stream-ordered,
+ * waits for completion and returns the status record.  Returns st->code (0 = OK). */
 int llmx_task(llmx_ctx *ctx, uint32_t op, uint32_t layer, uint32_t position,
               uint32_t rows, llmx_status *st);
+/* run_feature host:1088-1130: one feature operator (1-10) on host rows.
+ * lhs [rows][lhs_cols] with lhs_cols == in_dim; rhs (RMSNorm: the [1][hidden]
+ * weight row; SiLU-Mul: up rows; residual add: the second rows) [rhs_rows][rhs_cols];
+ * out [rows][out_cols] with out_cols == out_dim.  Projections use layer's
+ * weights (golden_projection host:3105-3142: exact sum, one double rounding);
+ * RMSNorm, SiLU-Mul and the residual add are the resident path's own kernels.
+ * Shape mismatches (the reference's runtime_error) return LLMX_ERR_ARG before
+ * any launch; controller codes come back in st->code.  Single-GPU contexts
+ * only (LLMX_ERR_UNSUPPORTED on a tensor-parallel rank). */
+int llmx_run_feature(llmx_ctx *ctx, uint32_t op, const int16_t *lhs, uint32_t rows,
+                     uint32_t lhs_cols, const int16_t *rhs, uint32_t rhs_rows,
+                     uint32_t rhs_cols, uint32_t layer, uint32_t position, int16_t *out,
+                     uint32_t out_cols, llmx_status *st);
+/* run_prefill_attention_block host:1647-1690 (op 17): attention of `rows`
+ * consecutive query tokens at positions position..position+rows-1 against
+ * layer's KV cache (which already holds those rows, e.g. via llmx_write_kv),
+ * causal per token.  query / out: kv_heads ports, port p = [rows][G][head_dim]
+ * of the G query heads of KV head p (token-major, then local head; ports back
+ * to back).  Same arithmetic as Task 18's attention.  Single-GPU only. */
+int llmx_run_prefill_attention_block(llmx_ctx *ctx, const int16_t *query, uint32_t position,
+                                     uint32_t rows, uint32_t layer, int16_t *out,
+                                     llmx_status *st);
 /* run_composed_decoder_stack host:1258-1493: host rows in -> layers
  * [layer_begin, layer_begin+layer_count) as Task 18/19 pairs -> optional
  * Task 20 -> optional host rows out.  Launched as one CUDA graph (cached per

@@ -21,7 +21,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off",
           "-I", os.path.join(ROOT, "include"), "-I", CSRC]
-SOURCES = ["kernels.cu", "gemv.cu", "attention.cu", "mma_proj.cu", "lm_head.cu", "runtime.cu", "host_model.cpp", "shape.cpp"]
+SOURCES = ["kernels.cu", "gemv.cu", "attention.cu", "mma_proj.cu", "lm_head.cu", "feature.cu", "runtime.cu", "host_model.cpp",
+           "shape.cpp"]
 
 
 def _nccl():

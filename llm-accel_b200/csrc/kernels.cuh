@@ -91,6 +91,14 @@ struct ProjArgs {
     uint32_t ar_off;     // EPI_PARTIAL: all-reduce number = step->ar_base + ar_off
     ArInput in;          // activation rows from a peer all-reduce (in.ar.n > 1) instead of x
     int row0;            // first row of this launch (x / out / resid already offset)
+    // L2 warm-up, once this CTA has issued its last weight copy (HBM would idle
+    // while the ring drains): the first next_bytes of the slice that CTA
+    // blockIdx.x of the next projection streams (next_units units of
+    // next_unit_bytes over the same grid); next_w == nullptr: none
+    const char *next_w;
+    int next_units;
+    uint32_t next_unit_bytes;
+    uint32_t next_bytes;
 };
 
 // Tensor-core projection of blocks of 3..8 rows (mma_proj.cu): weights in
@@ -181,6 +189,34 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
     int n;
     const Step *step;
 };
+
+// Per-operator (feature) kernels, feature.cu.  Slot orders of the packed
+// layout: output column o of the operator is sum column feature_slot(o).
+enum SlotOrder : int {
+    kSlotIdentity = 0,   // O, Down
+    kSlotRopePairs = 1,  // Q, K, V: head h, pair i -> slots h*hd + 2i (i < hd/2), + 1 (i + hd/2)
+    kSlotEven = 2,       // Gate of the interleaved Gate/Up slots
+    kSlotOdd = 3         // Up
+};
+struct FeatureRoundArgs {  // out[r][o] = round_mac(sums[r][slot(o)])
+    const int64_t *sums;
+    int sum_stride;
+    int16_t *out;
+    int rows;
+    int n_out;
+    int order;
+    int hd;
+};
+struct FeatureVecArgs {  // out = silu ? SiLU(lhs) x rhs : sat16(lhs + rhs), n elements
+    const int16_t *lhs;
+    const int16_t *rhs;
+    int16_t *out;
+    const int16_t *etab;
+    int n;
+    int silu;
+};
+cudaError_t launch_feature_round(const FeatureRoundArgs &a, cudaStream_t s);
+cudaError_t launch_feature_vec(const FeatureVecArgs &a, cudaStream_t s);
 
 struct ArFinishArgs {  // wait for every rank's sums, add them, round, + residual
     ArPeers ar;

@@ -88,13 +88,18 @@ struct llmx_ctx {
     int32_t *slot_qkv = nullptr, *slot_o = nullptr, *slot_gu = nullptr, *slot_d = nullptr;
     int16_t *norms = nullptr, *rope = nullptr, *etab = nullptr, *ptab = nullptr;
     int16_t *kc = nullptr, *vc = nullptr;
-    int16_t *hid[2] = {nullptr, nullptr};
+    // hidden pairs 0 and 1 (bound by the caller) and 2, the sublayer boundary of
+    // the full-layer Task 16 (the input pair stays unchanged)
+    int16_t *hid[3] = {nullptr, nullptr, nullptr};
     int16_t *q = nullptr, *att = nullptr, *act = nullptr;
     int64_t *partial = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
     int gemv_warps = 16;  // consumer warps of a projection CTA at most (LLMX_GEMV_WARPS)
+    // per-CTA L2 warm-up of the next projection's slice at the end of Gate/Up (->
+    // Down) and Down (-> next layer's QKV), KiB (LLMX_NEXT_PF_KB; 0 = off)
+    int next_pf_kb = 0;
     // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_tile_kb
     // KiB per 64-position context tile from the layer's O weights on, at most
     // attn_pf_kb KiB and the end of Gate/Up (LLMX_ATTN_PREFETCH_TILE_KB, _KB, _ROWS).
@@ -132,6 +137,9 @@ struct llmx_ctx {
     int32_t *mma_rows[4] = {nullptr, nullptr, nullptr, nullptr};
     int32_t inv_elems = 0, inv_rms_const = 0, qk_scale = 0;
     uint32_t out_pair = 0, in_pair = 1;
+    // per-operator (feature) calls: operand rows and exact sums, allocated on first use
+    int16_t *feat_lhs = nullptr, *feat_rhs = nullptr, *feat_out = nullptr;
+    int64_t *feat_sums = nullptr;
     std::vector<bool> layer_loaded;
     bool norms_loaded = false;
     uint64_t launches = 0, last_launches = 0, device_bytes = 0;
@@ -429,6 +437,11 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
     const int16_t *in = c->hid[in_pair];
     int16_t *out = c->hid[out_pair];
     const int ge = c->size > 1 ? EPI_PARTIAL : EPI_RESID;
+    if (op == LLMX_OP_DECODER_LAYER) {  // Task 18 into pair 2, then Task 19 from it
+        int rc = enqueue_task(c, LLMX_OP_ATTENTION_SUBLAYER, layer, rows, in_pair, 2, ar_next, fuse, pend);
+        if (!rc) rc = enqueue_task(c, LLMX_OP_FFN_SUBLAYER, layer, rows, 2, out_pair, ar_next, fuse, pend);
+        return rc;
+    }
     if (op == LLMX_OP_ATTENTION_SUBLAYER) {
         ProjArgs a = qkv_args(c, layer, in);
         take_input(c, a, pend);
@@ -458,6 +471,18 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         take_input(c, g, pend);
         ProjArgs d = down_args(c, layer, out, in);
         d.ar_off = ar_next;
+        if (c->next_pf_kb) {
+            g.next_w = reinterpret_cast<const char *>(d.w);  // Down rows of this layer
+            g.next_units = s.hidden;
+            g.next_unit_bytes = (uint32_t)c->Il * 2;
+            g.next_bytes = (uint32_t)c->next_pf_kb << 10;
+            if (layer + 1 < (uint32_t)s.layers) {  // the next layer's Q/K/V pairs
+                d.next_w = reinterpret_cast<const char *>(wl(c, layer + 1));
+                d.next_units = (c->Hq + 2 * c->KV) / 2;  // units of one RoPE pair (2 rows)
+                d.next_unit_bytes = (uint32_t)s.hidden * 2 * 2;
+                d.next_bytes = (uint32_t)c->next_pf_kb << 10;
+            }
+        }
         if (use_mma(c, rows, MP_GU)) {
             const int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
             if (rc) return rc;
@@ -502,7 +527,9 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
 
 // All-reduces of one coarse task / one stack (tensor parallel).
 uint32_t task_allreduces(const llmx_ctx *c, uint32_t op) {
-    return c->size > 1 && (op == LLMX_OP_ATTENTION_SUBLAYER || op == LLMX_OP_FFN_SUBLAYER) ? 1u : 0u;
+    if (c->size == 1) return 0u;
+    if (op == LLMX_OP_DECODER_LAYER) return 2u;
+    return op == LLMX_OP_ATTENTION_SUBLAYER || op == LLMX_OP_FFN_SUBLAYER ? 1u : 0u;
 }
 uint32_t stack_allreduces(const llmx_ctx *c, uint32_t layer_count) { return c->size > 1 ? 2u * layer_count : 0u; }
 
@@ -714,6 +741,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
+    c->next_pf_kb = env_int("LLMX_NEXT_PF_KB", 0, 0, 1024);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
     auto bail = [&](int code) {
         release(c);
@@ -764,7 +792,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->rope, (size_t)s.max_seq * hd)) || (rc = dalloc(c, &c->etab, 2049)) ||
         (rc = dalloc(c, &c->ptab, 2049)) || (rc = dalloc(c, &c->kc, kv_elems)) ||
         (rc = dalloc(c, &c->vc, kv_elems)) || (rc = dalloc(c, &c->hid[0], kMaxRows * H)) ||
-        (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
+        (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->hid[2], kMaxRows * H)) ||
+        (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->att, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->act, kMaxRows * (size_t)c->Il)) || (rc = dalloc(c, &c->partial, kMaxRows * H)) ||
         (rc = dalloc(c, &c->step, 1)) || (rc = dalloc(c, &c->err, 1)))
@@ -1022,6 +1051,148 @@ int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint3
     CK(cudaStreamSynchronize(c->stream));
     c->last_launches = c->launches - before;
     return check_device_error(c);
+}
+
+// Per-operator (feature) modes, ops 1-10 (run_feature host:1088-1130).
+int llmx_run_feature(llmx_ctx *c, uint32_t op, const int16_t *lhs, uint32_t rows, uint32_t lhs_cols,
+                     const int16_t *rhs, uint32_t rhs_rows, uint32_t rhs_cols, uint32_t layer, uint32_t position,
+                     int16_t *out, uint32_t out_cols, llmx_status *st) {
+    llmx_status local;
+    if (!st) st = &local;
+    if (!c || !lhs || !out) return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s;
+    uint32_t in_dim = 0, out_dim = 0;
+    int needs_rhs = 0;
+    if (llmx_feature_dims(&s, op, &in_dim, &out_dim, &needs_rhs) != LLMX_OK) {
+        g_last_error = "operator is not a feature operator";
+        return LLMX_ERR_ARG;
+    }
+    // the host's shape checks (runtime_error in the reference) come before any launch
+    if (rows == 0 || rows > LLMX_MAX_ROWS || lhs_cols != in_dim || out_cols != out_dim) {
+        g_last_error = "feature operator input shape mismatch";
+        return LLMX_ERR_ARG;
+    }
+    if (needs_rhs && (!rhs || rhs_cols != in_dim || rhs_rows != (op == LLMX_OP_RMSNORM ? 1u : rows))) {
+        g_last_error = "feature operator RHS shape mismatch";
+        return LLMX_ERR_ARG;
+    }
+    if (c->size > 1) {
+        g_last_error = "feature operators run on single-GPU contexts";
+        return LLMX_ERR_UNSUPPORTED;
+    }
+    const int code = llmx_validate_operator(&s, op, layer, position, rows, st);
+    if (code != LLMX_OK) return code;
+    const bool projection = op <= LLMX_OP_FFN_DOWN;
+    if (projection && !c->layer_loaded[layer]) return LLMX_ERR_STATE;
+    CK(cudaSetDevice(c->dev));
+    const size_t width = (size_t)std::max(s.hidden, s.inter);
+    const size_t slots = std::max<size_t>({(size_t)c->Hq + 2 * c->KV, (size_t)2 * c->Il, (size_t)s.hidden});
+    int rc = LLMX_OK;
+    if (!c->feat_lhs && ((rc = dalloc(c, &c->feat_lhs, kMaxRows * width)) ||
+                         (rc = dalloc(c, &c->feat_rhs, kMaxRows * width)) ||
+                         (rc = dalloc(c, &c->feat_out, kMaxRows * width)) ||
+                         (rc = dalloc(c, &c->feat_sums, kMaxRows * slots))))
+        return rc;
+    const uint64_t before = c->launches;
+    CK(cudaMemcpyAsync(c->feat_lhs, lhs, (size_t)rows * in_dim * 2, cudaMemcpyHostToDevice, c->stream));
+    if (needs_rhs)
+        CK(cudaMemcpyAsync(c->feat_rhs, rhs, (size_t)rhs_rows * in_dim * 2, cudaMemcpyHostToDevice, c->stream));
+    if ((rc = set_step(c, position, rows))) return rc;
+    if (projection) {
+        // the operator's slots of the packed layer blob: [slot0, slot0 + nslots) of
+        // a region whose rows are K inputs long
+        const uint32_t *w = wl(c, layer);
+        uint32_t K = s.hidden, slot0 = 0, nslots = 0;
+        int order = kSlotIdentity;
+        switch (op) {
+        case LLMX_OP_Q_PROJECTION: nslots = c->Hq, order = kSlotRopePairs; break;
+        case LLMX_OP_K_PROJECTION: slot0 = c->Hq, nslots = c->KV, order = kSlotRopePairs; break;
+        case LLMX_OP_V_PROJECTION: slot0 = c->Hq + c->KV, nslots = c->KV, order = kSlotRopePairs; break;
+        case LLMX_OP_O_PROJECTION: w += c->w_qkv, K = c->Hq, nslots = s.hidden; break;
+        case LLMX_OP_FFN_GATE:
+        case LLMX_OP_FFN_UP:
+            w += c->w_qkv + c->w_o, nslots = 2 * c->Il;
+            order = op == LLMX_OP_FFN_GATE ? kSlotEven : kSlotOdd;
+            break;
+        default: w += c->w_qkv + c->w_o + c->w_gu, K = c->Il, nslots = s.hidden; break;  // Down
+        }
+        const int rt = rows_template(rows);
+        ProjArgs a{};
+        a.w = w + (size_t)slot0 * (K / 2);
+        a.K = (int)K;
+        a.npairs = (int)nslots / 2;
+        a.x = c->feat_lhs;
+        a.step = c->step;
+        a.partial = c->feat_sums;
+        a.out_stride = (int)nslots;
+        set_stages(c, a, EPI_PARTIAL, rt);
+        CK(launch_proj(a, EPI_PARTIAL, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
+        FeatureRoundArgs f{c->feat_sums, (int)nslots, c->feat_out, (int)rows, (int)out_dim, order, c->hd};
+        CK(launch_feature_round(f, c->stream));
+        c->launches += 2;
+    } else if (op == LLMX_OP_RMSNORM) {
+        NormArgs n{c->feat_lhs, c->feat_rhs, c->feat_out, s.hidden, c->inv_elems, c->inv_rms_const, c->step};
+        CK(launch_rmsnorm(n, (int)rows, c->stream));
+        c->launches += 1;
+    } else {
+        FeatureVecArgs v{c->feat_lhs, c->feat_rhs, c->feat_out, c->etab, (int)(rows * in_dim),
+                         op == LLMX_OP_SILU_MUL ? 1 : 0};
+        CK(launch_feature_vec(v, c->stream));
+        c->launches += 1;
+    }
+    CK(cudaMemcpyAsync(out, c->feat_out, (size_t)rows * out_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->last_launches = c->launches - before;
+    return check_device_error(c);
+}
+
+// Prefill block attention, op 17 (run_prefill_attention_block host:1647-1690).
+int llmx_run_prefill_attention_block(llmx_ctx *c, const int16_t *query, uint32_t position, uint32_t rows,
+                                     uint32_t layer, int16_t *out, llmx_status *st) {
+    llmx_status local;
+    if (!st) st = &local;
+    if (!c || !query || !out) return LLMX_ERR_ARG;
+    const llmx_shape &s = c->s;
+    if (c->size > 1) {
+        g_last_error = "the prefill block operator runs on single-GPU contexts";
+        return LLMX_ERR_UNSUPPORTED;
+    }
+    // host:1655-1666: shape checks before the launch
+    if (rows == 0 || rows > LLMX_MAX_ROWS || (uint64_t)position + rows > (uint64_t)s.max_seq) {
+        g_last_error = "prefill attention block shape mismatch";
+        return LLMX_ERR_ARG;
+    }
+    const int code = llmx_validate_operator(&s, LLMX_OP_ATTN_PREFILL_BLOCK, layer, position, rows, st);
+    if (code != LLMX_OK) return code;
+    CK(cudaSetDevice(c->dev));
+    // ports (KV head p: [rows][G][hd], token-major then local head) <-> rows of all
+    // query heads [rows][heads][hd] (head = p * G + g): the host's pack_tight step
+    const int hd = c->hd, G = c->G, KVh = s.kv_heads, Hq = c->Hq;
+    std::vector<int16_t> rowbuf((size_t)rows * Hq);
+    for (int p = 0; p < KVh; p++)
+        for (uint32_t r = 0; r < rows; r++)
+            for (int g = 0; g < G; g++)
+                std::memcpy(&rowbuf[(size_t)r * Hq + (size_t)(p * G + g) * hd],
+                            query + (((size_t)p * rows + r) * G + g) * hd, (size_t)hd * 2);
+    const uint64_t before = c->launches;
+    CK(cudaMemcpyAsync(c->q, rowbuf.data(), rowbuf.size() * 2, cudaMemcpyHostToDevice, c->stream));
+    int rc = set_step(c, position, rows);
+    if (rc) return rc;
+    AttnArgs t = attn_args(c, layer);
+    t.pf_bytes = 0;  // no projection follows
+    t.pf_per_tile = 0;
+    CK(launch_attention(c, t, rows));
+    c->launches += 1;
+    CK(cudaMemcpyAsync(rowbuf.data(), c->att, rowbuf.size() * 2, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->last_launches = c->launches - before;
+    if ((rc = check_device_error(c))) return rc;
+    for (int p = 0; p < KVh; p++)
+        for (uint32_t r = 0; r < rows; r++)
+            for (int g = 0; g < G; g++)
+                std::memcpy(out + (((size_t)p * rows + r) * G + g) * hd,
+                            &rowbuf[(size_t)r * Hq + (size_t)(p * G + g) * hd], (size_t)hd * 2);
+    return LLMX_OK;
 }
 
 int llmx_stack_async(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t layer_count, uint32_t position,

@@ -55,6 +55,93 @@ int32_t qk_scale_q1616(int head_dim) {
 
 using namespace llmx;
 
+namespace {
+
+// Controller argument validation and the status record of a completed task
+// (kernel/control_cache_8x64.cpp:5869-5972, then the per-operator checks of
+// Task 20 :5974-5984, the resident layer tasks :6031-6054, the prefill block
+// :6496-6522 and the legacy feature scheduler :7273-7497).  full == false is
+// the production resident-layer image: every operator other than NOP and Tasks
+// 16, 18, 19, 20 is rejected (:6484-6494).  full == true is the image with the
+// per-operator schedulers; of those this library serves ops 1-10 and 17, and
+// answers the tile-diagnostic ops 11-15 as the resident image does.
+int validate_op(const llmx_shape *s, uint32_t op, uint32_t layer, uint32_t position, uint32_t rows,
+                llmx_status *st, bool full) {
+    if (!s || !st) return LLMX_ERR_ARG;
+    std::memset(st, 0, sizeof(*st));
+    st->op = LLMX_OP_NOP;
+    st->token_count = rows;
+    st->last_task = 1;
+    // :5891-5897: row count first, before the operator
+    if (rows > LLMX_MAX_ROWS) return st->code = LLMX_BAD_TOKEN_COUNT;
+    st->op = op;
+    const bool resident = op == LLMX_OP_NOP || op == LLMX_OP_DECODER_LAYER || op == LLMX_OP_ATTENTION_SUBLAYER ||
+                          op == LLMX_OP_FFN_SUBLAYER || op == LLMX_OP_FINAL_NORM;
+    const bool feature = op >= LLMX_OP_Q_PROJECTION && op <= LLMX_OP_RESIDUAL_ADD;
+    if (!resident && !(full && (feature || op == LLMX_OP_ATTN_PREFILL_BLOCK))) return st->code = LLMX_BAD_OPERATOR;
+    if (op == LLMX_OP_NOP) return st->code = LLMX_OK;
+    if (layer >= (uint32_t)s->layers) return st->code = LLMX_BAD_LAYER;
+    const uint32_t H = s->hidden, I = s->inter, hd = s->hidden / s->heads;
+    const uint32_t KV = s->kv_heads * hd, G = s->heads / s->kv_heads;
+    const uint32_t pv_waves = cdiv(hd, 64);  // CC8_ATTN_PV_WAVES: 64 outputs per MM wave
+    if (feature) {
+        uint32_t in_dim = 0, out_dim = 0;
+        int rhs = 0;
+        llmx_feature_dims(s, op, &in_dim, &out_dim, &rhs);
+        if (op <= LLMX_OP_FFN_DOWN) {  // one projection: 128 outputs per wave on both cores
+            const uint32_t waves = cdiv(out_dim, 128);
+            st->output_waves = waves;
+            st->mm_tasks = 2 * waves;
+            st->completed_packets = waves * 2 * 32;
+        } else {  // vector operator: tokens 0-3 on core 0, 4-7 on core 1
+            st->vector_tasks = (rows > 0 ? 1u : 0u) + (rows > 4 ? 1u : 0u);
+            st->completed_packets = rows * cdiv(out_dim, 16);
+        }
+        return st->code = LLMX_OK;
+    }
+    if (rows == 0) return st->code = LLMX_BAD_TOKEN_COUNT;
+    if (op != LLMX_OP_FINAL_NORM &&
+        (position >= (uint32_t)s->max_seq || (uint64_t)position + rows > (uint64_t)s->max_seq))
+        return st->code = LLMX_BAD_POSITION;
+    // status counters of a completed task (tests/closed_loop_8x64_cosim_tb.cpp:523-626)
+    const uint32_t fanout = cdiv(rows, 4);
+    uint32_t waves = 0, vec = 0, packets = 0;
+    if (op == LLMX_OP_ATTENTION_SUBLAYER || op == LLMX_OP_DECODER_LAYER) {
+        uint32_t w = cdiv(H, 128) + 2 * cdiv(KV, 128) + cdiv(H, 128);
+        for (uint32_t t = 0; t < rows; t++) w += cdiv((uint64_t)position + t + 1, 64) * (1 + pv_waves);
+        waves += w;
+        vec += 2 * fanout;
+        packets += w * 2 * 32 + 2 * rows * cdiv(H, 16);
+    }
+    if (op == LLMX_OP_FFN_SUBLAYER || op == LLMX_OP_DECODER_LAYER) {
+        const uint32_t w = 2 * cdiv(I, 128) + cdiv(H, 128);
+        waves += w;
+        vec += 3 * fanout;
+        packets += w * 2 * 32 + rows * (2 * cdiv(H, 16) + cdiv(I, 16));
+    }
+    if (op == LLMX_OP_FINAL_NORM) {
+        vec = fanout;
+        packets = rows * cdiv(H, 16);
+    }
+    if (op == LLMX_OP_ATTN_PREFILL_BLOCK) {
+        // :6511-6522 and check_prefill_block_attention_status host:5587-5604: every
+        // context tile runs QK plus the PV waves for each GQA head on both cores
+        // (the per-launch task limit is never reached for position + rows <= max_seq)
+        const uint32_t tasks_per_core = cdiv((uint64_t)position + rows, 64) * G * (1 + pv_waves);
+        st->output_waves = pv_waves;
+        st->mm_tasks = 2 * tasks_per_core;
+        st->completed_packets = st->mm_tasks * 32;
+        return st->code = LLMX_OK;
+    }
+    st->output_waves = waves;
+    st->mm_tasks = 2 * waves;
+    st->vector_tasks = vec;
+    st->completed_packets = packets;
+    return st->code = LLMX_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int llmx_profile(const char *name, llmx_shape *out) {
@@ -97,46 +184,33 @@ int llmx_shape_validate(const llmx_shape *s) {
 
 int llmx_validate_task(const llmx_shape *s, uint32_t op, uint32_t layer, uint32_t position, uint32_t rows,
                        llmx_status *st) {
-    if (!s || !st) return LLMX_ERR_ARG;
-    std::memset(st, 0, sizeof(*st));
-    st->op = LLMX_OP_NOP;
-    st->token_count = rows;
-    st->last_task = 1;
-    // kernel/control_cache_8x64.cpp:5891-5897: row count first, before the operator
-    if (rows > LLMX_MAX_ROWS) return st->code = LLMX_BAD_TOKEN_COUNT;
-    st->op = op;
-    // only the coarse resident tasks (and NOP) are served by this path
-    if (op != LLMX_OP_NOP && op != LLMX_OP_ATTENTION_SUBLAYER && op != LLMX_OP_FFN_SUBLAYER &&
-        op != LLMX_OP_FINAL_NORM)
-        return st->code = LLMX_BAD_OPERATOR;
-    if (op == LLMX_OP_NOP) return st->code = LLMX_OK;
-    if (layer >= (uint32_t)s->layers) return st->code = LLMX_BAD_LAYER;
-    if (rows == 0) return st->code = LLMX_BAD_TOKEN_COUNT;
-    if (op != LLMX_OP_FINAL_NORM &&
-        (position >= (uint32_t)s->max_seq || (uint64_t)position + rows > (uint64_t)s->max_seq))
-        return st->code = LLMX_BAD_POSITION;
-    // status counters of a completed task (tests/closed_loop_8x64_cosim_tb.cpp:523-626)
-    const uint32_t H = s->hidden, I = s->inter, hd = s->hidden / s->heads;
-    const uint32_t KV = s->kv_heads * hd;
-    const uint32_t fanout = cdiv(rows, 4);
-    if (op == LLMX_OP_ATTENTION_SUBLAYER) {
-        uint32_t waves = cdiv(H, 128) + 2 * cdiv(KV, 128) + cdiv(H, 128);
-        for (uint32_t t = 0; t < rows; t++) waves += cdiv((uint64_t)position + t + 1, 64) * (1 + cdiv(hd, 64));
-        st->output_waves = waves;
-        st->mm_tasks = 2 * waves;
-        st->vector_tasks = 2 * fanout;
-        st->completed_packets = waves * 2 * 32 + 2 * rows * cdiv(H, 16);
-    } else if (op == LLMX_OP_FFN_SUBLAYER) {
-        const uint32_t waves = 2 * cdiv(I, 128) + cdiv(H, 128);
-        st->output_waves = waves;
-        st->mm_tasks = 2 * waves;
-        st->vector_tasks = 3 * fanout;
-        st->completed_packets = waves * 2 * 32 + rows * (2 * cdiv(H, 16) + cdiv(I, 16));
-    } else {
-        st->vector_tasks = fanout;
-        st->completed_packets = rows * cdiv(H, 16);
+    return validate_op(s, op, layer, position, rows, st, false);
+}
+
+int llmx_validate_operator(const llmx_shape *s, uint32_t op, uint32_t layer, uint32_t position, uint32_t rows,
+                           llmx_status *st) {
+    return validate_op(s, op, layer, position, rows, st, true);
+}
+
+int llmx_feature_dims(const llmx_shape *s, uint32_t op, uint32_t *in_dim, uint32_t *out_dim, int *needs_rhs) {
+    if (!s || !in_dim || !out_dim || !needs_rhs) return LLMX_ERR_ARG;
+    const uint32_t H = s->hidden, I = s->inter, KV = (uint32_t)s->kv_heads * (s->hidden / s->heads);
+    // feature_input_dim / feature_output_dim / needs_rhs host:2015-2061
+    switch (op) {
+    case LLMX_OP_Q_PROJECTION: *in_dim = H, *out_dim = H; break;
+    case LLMX_OP_K_PROJECTION:
+    case LLMX_OP_V_PROJECTION: *in_dim = H, *out_dim = KV; break;
+    case LLMX_OP_O_PROJECTION: *in_dim = H, *out_dim = H; break;
+    case LLMX_OP_FFN_GATE:
+    case LLMX_OP_FFN_UP: *in_dim = H, *out_dim = I; break;
+    case LLMX_OP_FFN_DOWN: *in_dim = I, *out_dim = H; break;
+    case LLMX_OP_RMSNORM:
+    case LLMX_OP_RESIDUAL_ADD: *in_dim = H, *out_dim = H; break;
+    case LLMX_OP_SILU_MUL: *in_dim = I, *out_dim = I; break;
+    default: return LLMX_ERR_ARG;  // "operator is not a feature operator"
     }
-    return st->code = LLMX_OK;
+    *needs_rhs = op == LLMX_OP_RMSNORM || op == LLMX_OP_SILU_MUL || op == LLMX_OP_RESIDUAL_ADD;
+    return LLMX_OK;
 }
 
 const char *llmx_strerror(int code) {

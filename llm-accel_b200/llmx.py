@@ -25,6 +25,11 @@ OK = 0
 BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 3, 4, 5
 ERR_CUDA, ERR_ARG, ERR_STATE, ERR_NCCL, ERR_RANGE, ERR_NOMEM, ERR_IO, ERR_UNSUPPORTED, ERR_TIMEOUT = range(100, 109)
 OP_NOP, OP_ATTENTION, OP_FFN, OP_FINAL_NORM = 0, 18, 19, 20
+# per-operator modes (operator_kind_t host:69-91)
+(OP_Q_PROJECTION, OP_K_PROJECTION, OP_V_PROJECTION, OP_O_PROJECTION, OP_FFN_GATE, OP_FFN_UP, OP_FFN_DOWN,
+ OP_RMSNORM, OP_SILU_MUL, OP_RESIDUAL_ADD) = range(1, 11)
+OP_DECODER_LAYER, OP_ATTN_PREFILL_BLOCK = 16, 17
+FEATURE_OPS = tuple(range(1, 11))
 AR_NONE, AR_NCCL, AR_PEER = 0, 1, 2
 MAX_ROWS = 8
 KERNEL_QKV, KERNEL_ATTN, KERNEL_O, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_FINAL_NORM = range(6)
@@ -81,6 +86,13 @@ def lib():
             "llmx_profile": (C.c_int, [C.c_char_p, sp]),
             "llmx_shape_validate": (C.c_int, [sp]),
             "llmx_validate_task": (C.c_int, [sp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, stp]),
+            "llmx_validate_operator": (C.c_int, [sp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, stp]),
+            "llmx_feature_dims": (C.c_int, [sp, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                            C.POINTER(C.c_int)]),
+            "llmx_run_feature": (C.c_int, [vp, C.c_uint32, i16p, C.c_uint32, C.c_uint32, vp, C.c_uint32,
+                                           C.c_uint32, C.c_uint32, C.c_uint32, i16p, C.c_uint32, stp]),
+            "llmx_run_prefill_attention_block": (C.c_int, [vp, i16p, C.c_uint32, C.c_uint32, C.c_uint32, i16p,
+                                                           stp]),
             "llmx_strerror": (C.c_char_p, [C.c_int]),
             "llmx_last_error": (C.c_char_p, []),
             "llmx_exp_tables": (C.c_int, [i16p, i16p]),
@@ -166,6 +178,21 @@ def validate_task(s: Shape, op, layer, position, rows):
     st = Status()
     code = lib().llmx_validate_task(C.byref(s), op, layer, position, rows, C.byref(st))
     return code, st
+
+
+def validate_operator(s: Shape, op, layer, position, rows):
+    """Validation of the controller image with the per-operator schedulers."""
+    st = Status()
+    code = lib().llmx_validate_operator(C.byref(s), op, layer, position, rows, C.byref(st))
+    return code, st
+
+
+def feature_dims(s: Shape, op):
+    """(in_dim, out_dim, needs_rhs) of a feature operator (host:2015-2061)."""
+    i, o, r = C.c_uint32(), C.c_uint32(), C.c_int()
+    check(lib().llmx_feature_dims(C.byref(s), op, C.byref(i), C.byref(o), C.byref(r)),
+          f"operator {op} is not a feature operator")
+    return i.value, o.value, bool(r.value)
 
 
 def exp_tables():
@@ -323,6 +350,44 @@ class Accelerator:
         if raise_on_error:
             check(rc, f"task {op}")
         return rc, st
+
+    def run_feature(self, op, lhs, rhs=None, layer=0, position=0):
+        """run_feature host:1088-1130: one feature operator (1-10) on rows of lhs.
+        Returns (out [rows][out_dim], status)."""
+        lhs = np.ascontiguousarray(lhs, np.int16)
+        if lhs.ndim != 2:
+            raise ValueError("lhs must be [rows][cols]")
+        try:
+            out_dim = feature_dims(self.shape, op)[1]
+        except LlmxError:
+            out_dim = 0
+        out = np.zeros((lhs.shape[0], max(out_dim, 1)), np.int16)
+        rp, rr, rc_ = None, 0, 0
+        if rhs is not None:
+            rhs = np.ascontiguousarray(rhs, np.int16)
+            if rhs.ndim == 1:
+                rhs = rhs.reshape(1, -1)
+            rp, rr, rc_ = rhs.ctypes.data, rhs.shape[0], rhs.shape[1]
+        st = Status()
+        rc = lib().llmx_run_feature(self.h, op, lhs.reshape(-1), lhs.shape[0], lhs.shape[1], rp, rr, rc_, layer,
+                                    position, out.reshape(-1), out_dim, C.byref(st))
+        check(rc, f"feature operator {op}")
+        return out, st
+
+    def run_prefill_attention_block(self, query, position, layer=0):
+        """run_prefill_attention_block host:1647-1690: query [kv_heads][rows][G][head_dim]
+        (post-RoPE) against the layer's KV cache; returns (out of the same shape, status)."""
+        s = self.shape
+        q = np.ascontiguousarray(query, np.int16)
+        G = s.heads // s.kv_heads
+        if q.ndim != 4 or q.shape[0] != s.kv_heads or q.shape[2] != G or q.shape[3] != s.head_dim:
+            raise ValueError("prefill attention block shape mismatch")
+        out = np.zeros_like(q)
+        st = Status()
+        rc = lib().llmx_run_prefill_attention_block(self.h, q.reshape(-1), position, q.shape[1], layer,
+                                                    out.reshape(-1), C.byref(st))
+        check(rc, "prefill attention block")
+        return out, st
 
     def stack(self, hidden, layer_begin=0, layer_count=None, position=0, include_final_norm=True,
               materialize=True):

@@ -46,7 +46,9 @@ def test_controller_validation_order(llmx):
     code, st = llmx.validate_task(s, 99, 0, 0, 9)
     assert code == llmx.BAD_TOKEN_COUNT and st.op == 0
     assert llmx.validate_task(s, 99, 0, 0, 1)[0] == llmx.BAD_OPERATOR
-    assert llmx.validate_task(s, 16, 0, 0, 1)[0] == llmx.BAD_OPERATOR  # legacy one-launch layer
+    assert llmx.validate_task(s, 16, 0, 0, 1)[0] == llmx.OK  # compatibility full-layer task (:6031-6036)
+    assert llmx.validate_task(s, 17, 0, 0, 1)[0] == llmx.BAD_OPERATOR  # per-operator modes: not this image
+    assert llmx.validate_task(s, 16, 0, 2041, 8)[0] == llmx.BAD_POSITION
     assert llmx.validate_task(s, 0, 999, 9999, 1)[0] == llmx.OK
     assert llmx.validate_task(s, 18, 36, 0, 1)[0] == llmx.BAD_LAYER
     assert llmx.validate_task(s, 20, 36, 0, 1)[0] == llmx.BAD_LAYER
