@@ -33,12 +33,12 @@
 #include "device_util.cuh"
 #include "fixed.cuh"
 #include "kernels.cuh"
+#include "gemv_common.cuh"
 
 namespace llmx {
 
 namespace cg = cooperative_groups;
 
-constexpr int kKvStride = 136;  // padded smem row (int16): 272 B, 16-B aligned, conflict-free LDS.128
 constexpr int kAttnThreads = 256;
 constexpr int kMaxHd = 128;
 
@@ -51,9 +51,20 @@ static __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 constexpr int kMaxTiles = kCluster * kMaxTilesPerCta;
+// the softmax exp table (2049 entries, padded to 2056 in device memory) moves
+// as 257 16-byte cp.async chunks
+constexpr int kPtabChunks = 257;
+constexpr int kErrAttnCopy = 3;  // device error code: a K/V copy did not complete in time
+
+// K rows and V rows of a CTA's positions arrive with one 1-D bulk copy each
+// (completion on an mbarrier): the rows are contiguous in the cache and stay
+// unpadded in shared memory (head_dim int16 per row).  Lane L of the QK loop
+// walks the 16-byte vectors of its row starting at vector L mod (head_dim/8),
+// so the eight lanes of a quarter warp read eight different bank groups.
+static __device__ __forceinline__ int rot_vec(int v, int vpr) { return v >= vpr ? v - vpr : v; }
 
 struct AttnSmem {      // carved out of dynamic shared memory
-    int16_t *kv;       // [tpc*64][kKvStride] raw Q8.8 K rows, then V rows, of the owned tiles
+    int16_t *kv;       // [tpc*64][hd] raw Q8.8 K rows, then V rows, of the owned tiles
     int16_t *ptab;     // [2049] softmax exp table
     int16_t *q;        // [hd]
     int16_t *sc;       // [tpc*64] scores, then Q2.14 probabilities
@@ -62,15 +73,16 @@ struct AttnSmem {      // carved out of dynamic shared memory
     int32_t *gsum;     // [kMaxTiles] every tile's sum (pushed)
     int32_t *gold;     // [kMaxTiles] every tile's rescale factor (pushed)
     int32_t *tsum;     // [tpc] owned tile sums (local accumulation)
+    uint64_t *bar;     // [2] completion of the K and of the V copy
 };
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[9]) {
+static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[10]) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
-    off[0] = b; b = align16(b + rows * kKvStride * 2);                       // kv
-    off[1] = b; b = align16(b + 2049 * 2);                                   // ptab
+    off[0] = b; b = align16(b + rows * kMaxHd * 2);                          // kv
+    off[1] = b; b = align16(b + kPtabChunks * 16);                           // ptab
     off[2] = b; b = align16(b + (size_t)kMaxHd * 2);                         // q
     off[3] = b; b = align16(b + rows * 2);                                   // sc
     off[4] = b; b = align16(b + (size_t)kMaxTiles * (kMaxHd / cl) * 2);      // tvr
@@ -78,12 +90,13 @@ static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t of
     off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
     off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
     off[8] = b; b = align16(b + (size_t)tpc * 4);                            // tsum
+    off[9] = b; b = align16(b + 2 * 8);                                      // bar
     (void)hd;
     return b;
 }
 
 size_t attn_smem_bytes(int tpc, int hd, int cluster) {
-    size_t off[9];
+    size_t off[10];
     return attn_layout(tpc, hd, cluster, off);
 }
 
@@ -96,7 +109,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int lh = blockIdx.x / C;  // local query head
     const int r = blockIdx.y;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;  // elements finalised per CTA
-    size_t off[9];
+    size_t off[10];
     attn_layout(a.tpc_max, hd, C, off);
     AttnSmem m;
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
@@ -108,12 +121,19 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     m.gsum = reinterpret_cast<int32_t *>(raw + off[6]);
     m.gold = reinterpret_cast<int32_t *>(raw + off[7]);
     m.tsum = reinterpret_cast<int32_t *>(raw + off[8]);
+    m.bar = reinterpret_cast<uint64_t *>(raw + off[9]);
 
-    // the exp table does not depend on the producer kernel
-    for (int i = threadIdx.x; i < 2049; i += blockDim.x) m.ptab[i] = a.ptab[i];
+    // the exp table and the step record do not depend on the producer kernel
+    for (int i = threadIdx.x; i < kPtabChunks; i += blockDim.x) cp_async16(m.ptab + 8 * i, a.ptab + 8 * i);
+    if (threadIdx.x == 0) {
+        mbar_init(m.bar, 1);
+        mbar_init(m.bar + 1, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    const Step st = load_step(a.step);
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    const Step st = *a.step;
     // every CTA of the cluster reaches both cluster barriers, also when it owns nothing
     const bool row_ok = r < st.rows;
     const int ctx = st.position + r + 1;
@@ -127,9 +147,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int16_t *kb = a.kc + ((size_t)kvh * a.max_seq + p_begin) * hd;
     const int16_t *vb = a.vc + ((size_t)kvh * a.max_seq + p_begin) * hd;
 
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        cp_async16(m.kv + pp * kKvStride + cc, kb + (size_t)pp * hd + cc);
+    const uint32_t kv_bytes = (uint32_t)npos * hd * 2;
+    if (threadIdx.x == 0 && npos > 0) {
+        mbar_expect_tx(m.bar, kv_bytes);
+        bulk_g2s(m.kv, kb, kv_bytes, m.bar);
     }
     if (npos > 0) {
         const uint4 *qsrc = reinterpret_cast<const uint4 *>(a.q + (size_t)r * a.q_heads * hd + (size_t)lh * hd);
@@ -142,6 +163,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     if (threadIdx.x == 0 && pf_n && !a.pf_late)
         l2_prefetch_slice(a.pf, pf_n, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     cp_async_wait_all();
+    if (npos > 0 && !mbar_wait(m.bar, 0)) atomicCAS(a.error, 0, kErrAttnCopy);
     __syncthreads();
 
     // ---- 1. scores; owned tile maxima pushed to every CTA of the cluster ----
@@ -150,9 +172,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     // of them leaves int32 and the in-order saturating bank equals sat32 of its
     // exact sum.  Each bank is therefore summed as two exact int32 halves (even /
     // odd 16-byte vectors, <= 16 products each), added in int64 and saturated once.
+    const int rot = (threadIdx.x & 31) % vpr;
     for (int pp = threadIdx.x; pp < npos; pp += blockDim.x) {
         const uint4 *qv = reinterpret_cast<const uint4 *>(m.q);
-        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * hd);
         int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
         auto add8 = [&](int32_t (&c)[4], const uint4 q, const uint4 k) {
             c[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
@@ -167,10 +190,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         int e8 = 0;
 #pragma unroll 2
         for (; e8 + 1 < vpr; e8 += 2) {
-            add8(b[0], qv[e8], kv[e8]);
-            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
+            const int v0 = rot_vec(e8 + rot, vpr), v1 = rot_vec(e8 + 1 + rot, vpr);
+            add8(b[0], qv[v0], kv[v0]);
+            add8(b[1], qv[v1], kv[v1]);
         }
-        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        if (e8 < vpr) {
+            const int v0 = rot_vec(e8 + rot, vpr);
+            add8(b[0], qv[v0], kv[v0]);
+        }
         int64_t t64 = 0;
 #pragma unroll
         for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
@@ -180,11 +207,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         m.sc[pp] = (int16_t)sc;
     }
     __syncthreads();  // K consumed: the buffer now receives V (overlaps the exchange below)
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        cp_async16(m.kv + pp * kKvStride + cc, vb + (size_t)pp * hd + cc);
+    if (threadIdx.x == 0 && npos > 0) {
+        mbar_expect_tx(m.bar + 1, kv_bytes);
+        bulk_g2s(m.kv, vb, kv_bytes, m.bar + 1);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     {   // tile maxima: one warp per owned tile
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int tl = warp; tl < nown; tl += blockDim.x >> 5) {
@@ -212,7 +238,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         m.sc[pp] = (int16_t)pr;
         atomicAdd(m.tsum + pp / kTile, pr * 4);  // Q2.14 -> Q16.16; <= 64 * 2^16, never saturates
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (npos > 0 && !mbar_wait(m.bar + 1, 0)) atomicCAS(a.error, 0, kErrAttnCopy);
     __syncthreads();
     for (int i = threadIdx.x; i < nown; i += blockDim.x) {  // tile sum + rescale factor -> every CTA
         const int t = t_begin + i;
@@ -236,14 +262,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
         int pp = pb;
         for (; pp + 3 < pe; pp += 4) {
-            b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
-            b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
-            b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
-            b3 += qk_prod(m.sc[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
+            b0 += qk_prod(m.sc[pp], q412(m.kv[pp * hd + e]));
+            b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * hd + e]));
+            b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * hd + e]));
+            b3 += qk_prod(m.sc[pp + 3], q412(m.kv[(pp + 3) * hd + e]));
         }
-        if (pp < pe) b0 += qk_prod(m.sc[pp], q412(m.kv[pp * kKvStride + e]));
-        if (pp + 1 < pe) b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
-        if (pp + 2 < pe) b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+        if (pp < pe) b0 += qk_prod(m.sc[pp], q412(m.kv[pp * hd + e]));
+        if (pp + 1 < pe) b1 += qk_prod(m.sc[pp + 1], q412(m.kv[(pp + 1) * hd + e]));
+        if (pp + 2 < pe) b2 += qk_prod(m.sc[pp + 2], q412(m.kv[(pp + 2) * hd + e]));
         int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
         ts = sat32(rnd((int64_t)ts * 1024, 16));
         const int16_t tv = (int16_t)sat16(rnd(ts, 8));
@@ -274,7 +300,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
 // exchange are those of k_attn above.
 // ---------------------------------------------------------------------------
 struct AttnRowsSmem {
-    int16_t *kv;    // [tpc*64][kKvStride]  K rows, then V rows, shared by the rows
+    int16_t *kv;    // [tpc*64][hd]  K rows, then V rows, shared by the rows
     int16_t *ptab;  // [2049]
     int16_t *q;     // [kMaxRows][hd]
     int16_t *sc;    // [kMaxRows][tpc*64]  scores, then probabilities
@@ -283,13 +309,14 @@ struct AttnRowsSmem {
     int32_t *gsum;  // [kMaxRows][kMaxTiles]
     int32_t *gold;  // [kMaxRows][kMaxTiles]
     int32_t *tsum;  // [kMaxRows][tpc]
+    uint64_t *bar;  // [2] completion of the K and of the V copy
 };
 
-static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[9]) {
+static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[10]) {
     const size_t P = (size_t)tpc * kTile;
     size_t b = 0;
-    off[0] = b; b = align16(b + P * kKvStride * 2);
-    off[1] = b; b = align16(b + 2049 * 2);
+    off[0] = b; b = align16(b + P * kMaxHd * 2);
+    off[1] = b; b = align16(b + kPtabChunks * 16);
     off[2] = b; b = align16(b + (size_t)kMaxRows * kMaxHd * 2);
     off[3] = b; b = align16(b + (size_t)kMaxRows * P * 2);
     off[4] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * (kMaxHd / cl) * 2);
@@ -297,11 +324,12 @@ static __host__ __device__ size_t attn_rows_layout(int tpc, int cl, size_t off[9
     off[6] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
     off[7] = b; b = align16(b + (size_t)kMaxRows * kMaxTiles * 4);
     off[8] = b; b = align16(b + (size_t)kMaxRows * tpc * 4);
+    off[9] = b; b = align16(b + 2 * 8);
     return b;
 }
 
 size_t attn_rows_smem_bytes(int tpc, int cluster) {
-    size_t off[9];
+    size_t off[10];
     return attn_rows_layout(tpc, cluster, off);
 }
 
@@ -314,7 +342,7 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     const int c = (int)cluster.block_rank();
     const int lh = blockIdx.x / C;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;
-    size_t off[9];
+    size_t off[10];
     attn_rows_layout(a.tpc_max, C, off);
     AttnRowsSmem m;
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
@@ -326,12 +354,19 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     m.gsum = reinterpret_cast<int32_t *>(raw + off[6]);
     m.gold = reinterpret_cast<int32_t *>(raw + off[7]);
     m.tsum = reinterpret_cast<int32_t *>(raw + off[8]);
+    m.bar = reinterpret_cast<uint64_t *>(raw + off[9]);
     const int P = a.tpc_max * kTile;  // row stride of sc
 
-    for (int i = threadIdx.x; i < 2049; i += blockDim.x) m.ptab[i] = a.ptab[i];
+    for (int i = threadIdx.x; i < kPtabChunks; i += blockDim.x) cp_async16(m.ptab + 8 * i, a.ptab + 8 * i);
+    if (threadIdx.x == 0) {
+        mbar_init(m.bar, 1);
+        mbar_init(m.bar + 1, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    const Step st = load_step(a.step);
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    const Step st = *a.step;
     const int R = st.rows;
     const int ntiles = (st.position + R + kTile - 1) / kTile;  // the longest row's tiles
     const int tpc = max(1, (ntiles + C - 1) / C);
@@ -345,9 +380,10 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     const int16_t *kb = a.kc + ((size_t)kvh * a.max_seq + p_begin) * hd;
     const int16_t *vb = a.vc + ((size_t)kvh * a.max_seq + p_begin) * hd;
 
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        cp_async16(m.kv + pp * kKvStride + cc, kb + (size_t)pp * hd + cc);
+    const uint32_t kv_bytes = (uint32_t)npos * hd * 2;
+    if (threadIdx.x == 0 && npos > 0) {
+        mbar_expect_tx(m.bar, kv_bytes);
+        bulk_g2s(m.kv, kb, kv_bytes, m.bar);
     }
     for (int i = threadIdx.x; i < R * vpr; i += blockDim.x) {
         const int r = i / vpr, v = i - r * vpr;
@@ -356,14 +392,16 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     }
     for (int i = threadIdx.x; i < R * tpc; i += blockDim.x) m.tsum[i] = 0;
     cp_async_wait_all();
+    if (npos > 0 && !mbar_wait(m.bar, 0)) atomicCAS(a.error, 0, kErrAttnCopy);
     __syncthreads();
 
     // ---- 1. scores of every (row, position) of the row's context -----------
+    const int rot = (threadIdx.x & 31) % vpr;
     for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
         const int r = i / npos, pp = i - r * npos;
         if (pp >= npos_of(r)) continue;
         const uint4 *qv = reinterpret_cast<const uint4 *>(m.q + r * kMaxHd);
-        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * kKvStride);
+        const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * hd);
         int32_t b[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
         auto add8 = [&](int32_t (&cc)[4], const uint4 q, const uint4 k) {
             cc[0] += qk_prod(lo16(q.x), q412(lo16(k.x)));
@@ -377,10 +415,14 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
         };
         int e8 = 0;
         for (; e8 + 1 < vpr; e8 += 2) {
-            add8(b[0], qv[e8], kv[e8]);
-            add8(b[1], qv[e8 + 1], kv[e8 + 1]);
+            const int v0 = rot_vec(e8 + rot, vpr), v1 = rot_vec(e8 + 1 + rot, vpr);
+            add8(b[0], qv[v0], kv[v0]);
+            add8(b[1], qv[v1], kv[v1]);
         }
-        if (e8 < vpr) add8(b[0], qv[e8], kv[e8]);
+        if (e8 < vpr) {
+            const int v0 = rot_vec(e8 + rot, vpr);
+            add8(b[0], qv[v0], kv[v0]);
+        }
         int64_t t64 = 0;
 #pragma unroll
         for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[0][j] + b[1][j]);
@@ -389,11 +431,10 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
         m.sc[r * P + pp] = (int16_t)sat16(rnd(tot, 8));
     }
     __syncthreads();  // K consumed: the buffer now receives V
-    for (int i = threadIdx.x; i < npos * vpr; i += blockDim.x) {
-        const int pp = i / vpr, cc = (i - pp * vpr) << 3;
-        cp_async16(m.kv + pp * kKvStride + cc, vb + (size_t)pp * hd + cc);
+    if (threadIdx.x == 0 && npos > 0) {
+        mbar_expect_tx(m.bar + 1, kv_bytes);
+        bulk_g2s(m.kv, vb, kv_bytes, m.bar + 1);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     {   // tile maxima of every (row, owned tile in the row's context): one warp each
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int w = warp; w < R * nown; w += blockDim.x >> 5) {
@@ -423,7 +464,7 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
         m.sc[r * P + pp] = (int16_t)pr;
         atomicAdd(m.tsum + r * tpc + pp / kTile, pr * 4);
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (npos > 0 && !mbar_wait(m.bar + 1, 0)) atomicCAS(a.error, 0, kErrAttnCopy);
     __syncthreads();
     for (int i = threadIdx.x; i < R * nown; i += blockDim.x) {
         const int r = i / nown, tl = i - r * nown, t = t_begin + tl;
@@ -448,14 +489,14 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
         int32_t b0 = 0, b1 = 0, b2 = 0, b3 = 0;
         int pp = pb;
         for (; pp + 3 < pe; pp += 4) {
-            b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
-            b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
-            b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
-            b3 += qk_prod(scr[pp + 3], q412(m.kv[(pp + 3) * kKvStride + e]));
+            b0 += qk_prod(scr[pp], q412(m.kv[pp * hd + e]));
+            b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * hd + e]));
+            b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * hd + e]));
+            b3 += qk_prod(scr[pp + 3], q412(m.kv[(pp + 3) * hd + e]));
         }
-        if (pp < pe) b0 += qk_prod(scr[pp], q412(m.kv[pp * kKvStride + e]));
-        if (pp + 1 < pe) b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * kKvStride + e]));
-        if (pp + 2 < pe) b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * kKvStride + e]));
+        if (pp < pe) b0 += qk_prod(scr[pp], q412(m.kv[pp * hd + e]));
+        if (pp + 1 < pe) b1 += qk_prod(scr[pp + 1], q412(m.kv[(pp + 1) * hd + e]));
+        if (pp + 2 < pe) b2 += qk_prod(scr[pp + 2], q412(m.kv[(pp + 2) * hd + e]));
         int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
         ts = sat32(rnd((int64_t)ts * 1024, 16));
         const int16_t tv = (int16_t)sat16(rnd(ts, 8));

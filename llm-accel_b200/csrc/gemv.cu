@@ -299,13 +299,6 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
                 if (j == S - 1) pdl_wait();  // ring primed before waiting on the producer kernel
             }
             if (nchunks < S) pdl_wait();
-            if (ok && a.next_w != nullptr && a.next_bytes) {
-                const int n0 = (int)((int64_t)a.next_units * blockIdx.x / gridDim.x);
-                const int n1 = (int)((int64_t)a.next_units * (blockIdx.x + 1) / gridDim.x);
-                const unsigned long long len =
-                    min((unsigned long long)a.next_bytes, (unsigned long long)(n1 - n0) * a.next_unit_bytes) & ~15ull;
-                if (len) l2_prefetch_slice(a.next_w + (size_t)n0 * a.next_unit_bytes, len, 0, 1);
-            }
             if (!ok) {
                 atomicExch(a.error, 1);
                 // drain: wait (bounded) for the last fill of every stage this thread issued
@@ -320,9 +313,9 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
 
     // ---------------- consumer warps ----------------------------------------
     const int tid = threadIdx.x;
+    const Step st = load_step(a.step);
     pdl_wait();
     pdl_trigger();
-    const Step st = *a.step;
     const int rows = st.rows - a.row0;  // rows of this launch (a block may be split in row groups)
     const uint32_t ar_n = st.ar_base + a.ar_off;  // EPI_PARTIAL: this projection's all-reduce
     stage_rows<R>(a, st, xs, rows, tid);

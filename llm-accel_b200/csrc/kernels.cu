@@ -30,10 +30,11 @@ cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, cudaS
 __global__ void __launch_bounds__(256) k_rmsnorm(const NormArgs a) {
     __shared__ int64_t red[8];
     __shared__ int32_t inv_s;
+    const int rows = load_step(a.step).rows;
     pdl_wait();
     pdl_trigger();
     const int r = blockIdx.x;
-    if (r >= a.step->rows) return;
+    if (r >= rows) return;
     const int16_t *x = a.x + (size_t)r * a.n;
     if (a.inv_elems == 0) {
         if (threadIdx.x == 0) inv_s = a.inv_rms_const;
@@ -65,9 +66,9 @@ cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s) {
 // tensor parallel: round the all-reduced exact sums and add the residual
 // --------------------------------------------------------------------------
 __global__ void k_round_resid(const ResidArgs a) {
+    const int rows = load_step(a.step).rows;
     pdl_wait();
     pdl_trigger();
-    const int rows = a.step->rows;
     const int total = rows * a.n;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x)
         a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(a.partial[i]));
@@ -79,12 +80,12 @@ __global__ void k_round_resid(const ResidArgs a) {
 // every rank, adds the ranks' exact sums (order-free), rounds as round_mac and
 // adds the residual -- the same result on every rank.
 __global__ void __launch_bounds__(256) k_ar_finish(const ArFinishArgs a) {
+    const Step st = load_step(a.step);
     pdl_wait();
     pdl_trigger();
     __shared__ int fail_s;
     if (threadIdx.x == 0) fail_s = 0;
     __syncthreads();
-    const Step st = *a.step;
     const uint32_t n = st.ar_base + a.ar_off;
     const int H = a.ar.hidden;
     const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);  // 4 consecutive elements (H % 8 == 0)

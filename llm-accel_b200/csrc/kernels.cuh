@@ -19,6 +19,20 @@ struct Step {
     int32_t pad;
 };
 
+// The step record of the running call, read before griddepcontrol.wait: only
+// k_set_step writes it, with an ordinary (non-dependent) launch, so every
+// kernel of the call starts after that write has completed.  Read through L2
+// (ld.global.cg) so that no L1 line of an earlier call is seen.
+static __device__ __forceinline__ Step load_step(const Step *p) {
+    const int4 v = __ldcg(reinterpret_cast<const int4 *>(p));
+    Step s;
+    s.position = v.x;
+    s.rows = v.y;
+    s.ar_base = (uint32_t)v.z;
+    s.pad = v.w;
+    return s;
+}
+
 enum Epi : int {
     EPI_QKV = 0,   // RoPE on Q/K, Q -> q buffer, K/V -> KV cache
     EPI_RESID = 1, // + residual -> hidden out (O and Down projections)
@@ -91,14 +105,6 @@ struct ProjArgs {
     uint32_t ar_off;     // EPI_PARTIAL: all-reduce number = step->ar_base + ar_off
     ArInput in;          // activation rows from a peer all-reduce (in.ar.n > 1) instead of x
     int row0;            // first row of this launch (x / out / resid already offset)
-    // L2 warm-up, once this CTA has issued its last weight copy (HBM would idle
-    // while the ring drains): the first next_bytes of the slice that CTA
-    // blockIdx.x of the next projection streams (next_units units of
-    // next_unit_bytes over the same grid); next_w == nullptr: none
-    const char *next_w;
-    int next_units;
-    uint32_t next_unit_bytes;
-    uint32_t next_bytes;
 };
 
 // Tensor-core projection of blocks of 3..8 rows (mma_proj.cu): weights in
@@ -170,6 +176,7 @@ struct AttnArgs {
     unsigned long long pf_bytes;
     unsigned long long pf_per_tile;
     int pf_late;         // issue it after the first cluster barrier (K and V in shared memory)
+    int *error;          // device word: nonzero after a bounded wait expired
 };
 
 struct NormArgs {

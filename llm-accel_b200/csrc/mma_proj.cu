@@ -343,11 +343,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
         }
     } else {  // ---------------- warps 0, 2-5: activations, then MMA / epilogue ---------
         const int tid = warp == 0 ? lane : threadIdx.x - 32;  // 0..159
+        const Step st = load_step(a.step);
+        if (EPI == EPI_SILU)  // the SiLU table does not depend on the previous kernel either
+            for (int i = tid; i < 2049; i += 160) etab_s[i] = a.etab[i];
         pdl_wait();
         pdl_trigger();
-        const Step st = *a.step;
-        if (EPI == EPI_SILU)
-            for (int i = tid; i < 2049; i += 160) etab_s[i] = a.etab[i];
         mma_stage_rows(a, bsl, w0, n, st.rows, tid, 160, inv_s, red);
         named_sync(1, 160);
 

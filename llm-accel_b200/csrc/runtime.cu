@@ -97,9 +97,6 @@ struct llmx_ctx {
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
     int gemv_warps = 16;  // consumer warps of a projection CTA at most (LLMX_GEMV_WARPS)
-    // per-CTA L2 warm-up of the next projection's slice at the end of Gate/Up (->
-    // Down) and Down (-> next layer's QKV), KiB (LLMX_NEXT_PF_KB; 0 = off)
-    int next_pf_kb = 0;
     // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_tile_kb
     // KiB per 64-position context tile from the layer's O weights on, at most
     // attn_pf_kb KiB and the end of Gate/Up (LLMX_ATTN_PREFETCH_TILE_KB, _KB, _ROWS).
@@ -261,6 +258,7 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.tpc_max = c->tpc_max;
     t.cluster = kCluster;
     t.qk_scale = c->qk_scale;
+    t.error = c->err;
     // O then Gate/Up follow the QKV words of the layer blob
     t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
     t.pf_bytes = (c->w_o + c->w_gu) * 4ull;
@@ -471,18 +469,6 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         take_input(c, g, pend);
         ProjArgs d = down_args(c, layer, out, in);
         d.ar_off = ar_next;
-        if (c->next_pf_kb) {
-            g.next_w = reinterpret_cast<const char *>(d.w);  // Down rows of this layer
-            g.next_units = s.hidden;
-            g.next_unit_bytes = (uint32_t)c->Il * 2;
-            g.next_bytes = (uint32_t)c->next_pf_kb << 10;
-            if (layer + 1 < (uint32_t)s.layers) {  // the next layer's Q/K/V pairs
-                d.next_w = reinterpret_cast<const char *>(wl(c, layer + 1));
-                d.next_units = (c->Hq + 2 * c->KV) / 2;  // units of one RoPE pair (2 rows)
-                d.next_unit_bytes = (uint32_t)s.hidden * 2 * 2;
-                d.next_bytes = (uint32_t)c->next_pf_kb << 10;
-            }
-        }
         if (use_mma(c, rows, MP_GU)) {
             const int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
             if (rc) return rc;
@@ -741,7 +727,6 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
-    c->next_pf_kb = env_int("LLMX_NEXT_PF_KB", 0, 0, 1024);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
     auto bail = [&](int code) {
         release(c);
@@ -784,13 +769,14 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->w_d = H * (size_t)c->Il / 2;
     c->layer_words = c->w_qkv + c->w_o + c->w_gu + c->w_d;
     const size_t kv_elems = (size_t)s.layers * s.kv_heads * s.max_seq * hd;
+    // the softmax table (2049 entries) is padded to 2056: attention copies it in 16-byte chunks
     if ((rc = dalloc(c, &c->wbuf, c->layer_words * s.layers)) ||
         (rc = dalloc(c, &c->staging, layer_elems(s))) ||
         (rc = dalloc(c, &c->slot_qkv, c->Hq + 2 * c->KV)) || (rc = dalloc(c, &c->slot_o, H)) ||
         (rc = dalloc(c, &c->slot_gu, 2 * c->Il)) || (rc = dalloc(c, &c->slot_d, H)) ||
         (rc = dalloc(c, &c->norms, (2 * (size_t)s.layers + 1) * H)) ||
         (rc = dalloc(c, &c->rope, (size_t)s.max_seq * hd)) || (rc = dalloc(c, &c->etab, 2049)) ||
-        (rc = dalloc(c, &c->ptab, 2049)) || (rc = dalloc(c, &c->kc, kv_elems)) ||
+        (rc = dalloc(c, &c->ptab, 2056)) || (rc = dalloc(c, &c->kc, kv_elems)) ||
         (rc = dalloc(c, &c->vc, kv_elems)) || (rc = dalloc(c, &c->hid[0], kMaxRows * H)) ||
         (rc = dalloc(c, &c->hid[1], kMaxRows * H)) || (rc = dalloc(c, &c->hid[2], kMaxRows * H)) ||
         (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
