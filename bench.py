@@ -259,6 +259,9 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
     # every kernel of a decode layer at context P + 1 on this rank (no all-reduce in these launches)
     kernel_us = {n: acc.time_kernel(i, 0, P, 1, 2 * L) * 1e3
                  for i, n in enumerate(["qkv", "attention", "o_proj", "gate_up", "down", "final_norm"])}
+    if acc.decode_fuses_o:  # the decode layer's attention launch also does the O projection
+        kernel_us["attention_with_o"] = kernel_us.pop("attention")
+        kernel_us.pop("o_proj")
     gu_ms = acc.time_kernel(llmx.KERNEL_GATE_UP, 0, P, 1, 3 * L)
     down_ms = acc.time_kernel(llmx.KERNEL_DOWN, 0, P, 1, 3 * L)
     gu_bytes = 2 * Il * H * 2 + H * 2 + H * 2 + Il * 2

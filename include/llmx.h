@@ -270,6 +270,11 @@ uint64_t llmx_device_bytes(const llmx_ctx *ctx);
                             could not map a peer's exchange region) */
 #define LLMX_AR_PEER 2   /* peer stores over NVLink, finished in the next projection's prologue */
 int llmx_allreduce_kind(const llmx_ctx *ctx);
+/* 1 when one-row stacks run the O projection inside the attention kernel (single
+ * GPU; LLMX_ATTN_FUSE_O=0 disables): each attention cluster adds its head's exact
+ * partial of every O row into int64 sums that the Gate/Up prologue rounds (with
+ * the residual), so a decode layer is four launches instead of five. */
+int llmx_decode_fuses_o(const llmx_ctx *ctx);
 /* Failure-detection self-test (no reference counterpart; the reference's
  * controller has no waits that can expire).  Runs the receiving side of the
  * peer all-reduce on an exchange region that no rank writes, with a wait of

@@ -73,15 +73,20 @@ struct AttnSmem {      // carved out of dynamic shared memory
     int32_t *gsum;     // [kMaxTiles] every tile's sum (pushed)
     int32_t *gold;     // [kMaxTiles] every tile's rescale factor (pushed)
     int32_t *tsum;     // [tpc] owned tile sums (local accumulation)
-    uint64_t *bar;     // [2] completion of the K and of the V copy
+    uint64_t *bar;     // [3] completion of the K, the V and the O-weight copies
+    int16_t *att;      // [hd] the head's output (fused O projection)
+    uint32_t *ow;      // [o_rows][hd/2] this CTA's O rows, the head's columns (fused O projection):
+                       // the K/V buffer, reused once PV is done
 };
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t off[10]) {
+static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, int o_rows, size_t off[12]) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
-    off[0] = b; b = align16(b + rows * kMaxHd * 2);                          // kv
+    // kv, later the O slice (the same bytes: the CTA count per SM stays that of
+    // attention alone, which keeps every cluster of the grid resident at once)
+    off[0] = b; b = align16(b + (rows > (size_t)o_rows ? rows : (size_t)o_rows) * kMaxHd * 2);
     off[1] = b; b = align16(b + kPtabChunks * 16);                           // ptab
     off[2] = b; b = align16(b + (size_t)kMaxHd * 2);                         // q
     off[3] = b; b = align16(b + rows * 2);                                   // sc
@@ -90,14 +95,16 @@ static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, size_t of
     off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
     off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
     off[8] = b; b = align16(b + (size_t)tpc * 4);                            // tsum
-    off[9] = b; b = align16(b + 2 * 8);                                      // bar
+    off[9] = b; b = align16(b + 3 * 8);                                      // bar
+    off[10] = b; b = align16(b + (size_t)kMaxHd * 2);                        // att
+    off[11] = off[0];                                                        // ow
     (void)hd;
     return b;
 }
 
-size_t attn_smem_bytes(int tpc, int hd, int cluster) {
-    size_t off[10];
-    return attn_layout(tpc, hd, cluster, off);
+size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows) {
+    size_t off[12];
+    return attn_layout(tpc, hd, cluster, o_rows, off);
 }
 
 
@@ -109,8 +116,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int lh = blockIdx.x / C;  // local query head
     const int r = blockIdx.y;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;  // elements finalised per CTA
-    size_t off[10];
-    attn_layout(a.tpc_max, hd, C, off);
+    size_t off[12];
+    attn_layout(a.tpc_max, hd, C, a.o_w != nullptr ? a.o_rows : 0, off);
     AttnSmem m;
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
     m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
@@ -122,20 +129,30 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     m.gold = reinterpret_cast<int32_t *>(raw + off[7]);
     m.tsum = reinterpret_cast<int32_t *>(raw + off[8]);
     m.bar = reinterpret_cast<uint64_t *>(raw + off[9]);
+    m.att = reinterpret_cast<int16_t *>(raw + off[10]);
+    m.ow = reinterpret_cast<uint32_t *>(raw + off[11]);
 
-    // the exp table and the step record do not depend on the producer kernel
+    // the exp table, the step record and the O weights do not depend on the producer kernel
     for (int i = threadIdx.x; i < kPtabChunks; i += blockDim.x) cp_async16(m.ptab + 8 * i, a.ptab + 8 * i);
+    const Step st = load_step(a.step);
+    const bool row_ok = r < st.rows;
+    // fused O projection: this CTA's o_rows O rows of the head's hd columns
+    // (contiguous in the head-major copy) are warmed into L2 now -- they do not
+    // depend on the producer kernel -- and copied into the K/V buffer once PV is done
+    const bool fuse_o = a.o_w != nullptr && row_ok;
+    const uint32_t ow_bytes = (uint32_t)a.o_rows * hd * 2;
+    const uint32_t *ow_src = a.o_w + ((size_t)lh * a.hidden + (size_t)c * a.o_rows) * (hd >> 1);
     if (threadIdx.x == 0) {
         mbar_init(m.bar, 1);
         mbar_init(m.bar + 1, 1);
+        mbar_init(m.bar + 2, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (fuse_o) l2_prefetch_slice(reinterpret_cast<const char *>(ow_src), ow_bytes, 0, 1);
     }
-    const Step st = load_step(a.step);
     __syncthreads();
     pdl_wait();
     pdl_trigger();
-    // every CTA of the cluster reaches both cluster barriers, also when it owns nothing
-    const bool row_ok = r < st.rows;
+    // every CTA of the cluster reaches every cluster barrier, also when it owns nothing
     const int ctx = st.position + r + 1;
     const int ntiles = row_ok ? (ctx + kTile - 1) / kTile : 0;
     const int tpc = max(1, (ntiles + C - 1) / C);
@@ -276,6 +293,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
     }
     cluster.sync();
+    if (fuse_o && threadIdx.x == 0) {  // V is consumed: the buffer now receives the O slice
+        mbar_expect_tx(m.bar + 2, ow_bytes);
+        bulk_g2s(m.ow, ow_src, ow_bytes, m.bar + 2);
+    }
 
     // ---- 3. in-order Q16.16 recurrence on local shared memory ---------------
     for (int j = threadIdx.x; ntiles > 0 && j < epc; j += blockDim.x) {
@@ -288,7 +309,45 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
             acc = sat32((int64_t)acc + (int64_t)m.tvr[u * epc + j] * 256);
         }
         const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
-        a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
+        const int16_t y = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
+        if (a.o_w == nullptr) {
+            a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = y;
+        } else {  // the head output -> every CTA of the cluster
+            for (int k = 0; k < C; k++) *cluster.map_shared_rank(m.att + e, k) = y;
+        }
+    }
+    if (a.o_w == nullptr) return;
+
+    // ---- 4. fused O projection: this head's exact partial of this CTA's O rows ----
+    // (golden_projection host:3105-3142 sums int16 x int16 products exactly and
+    // rounds once; the sum over heads is completed by int64 atomics and rounded,
+    // with the residual, by the next kernel's prologue)
+    cluster.sync();
+    if (!fuse_o) return;
+    if (!mbar_wait(m.bar + 2, 0)) {
+        atomicCAS(a.error, 0, kErrAttnCopy);
+        (void)mbar_wait(m.bar + 2, 0);  // give the copies a second bounded wait before leaving
+    }
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(m.att);
+    for (int j = threadIdx.x; j < a.o_rows; j += blockDim.x) {
+        const uint4 *w4 = reinterpret_cast<const uint4 *>(m.ow + (size_t)j * (hd >> 1));
+        int32_t lo = 0, hi = 0;  // <= 128 products: |lo| < 2^31, |hi| < 2^29
+        int v = rot;
+        for (int k = 0; k < vpr; k++) {
+            const uint4 w = w4[v], x = x4[v];
+            lo = dp2a_lo_su(x.x, w.x, lo);
+            hi = dp2a_hi_ss(x.x, w.x, hi);
+            lo = dp2a_lo_su(x.y, w.y, lo);
+            hi = dp2a_hi_ss(x.y, w.y, hi);
+            lo = dp2a_lo_su(x.z, w.z, lo);
+            hi = dp2a_hi_ss(x.z, w.z, hi);
+            lo = dp2a_lo_su(x.w, w.w, lo);
+            hi = dp2a_hi_ss(x.w, w.w, hi);
+            v = rot_vec(v + 1, vpr);
+        }
+        const int64_t tot = (int64_t)hi * 256 + lo;
+        atomicAdd(reinterpret_cast<unsigned long long *>(a.o_acc + (size_t)r * a.hidden + (size_t)c * a.o_rows + j),
+                  (unsigned long long)tot);
     }
 }
 
@@ -565,7 +624,7 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cluster * a.q_heads, rows);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster);
+    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster, a.o_w != nullptr ? a.o_rows : 0);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

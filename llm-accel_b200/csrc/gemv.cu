@@ -77,6 +77,45 @@ static __device__ void stage_rows_allreduce(const ProjArgs &a, const Step &st, i
     consumer_sync();
 }
 
+// Rows of the fused attention + O projection -> shared memory (raw, before any
+// norm): x = sat16(resid + round(sum)) from the exact O sums the attention
+// kernel added up (the rounding and residual of the O projection's epilogue).
+// Block 0 also writes the rows to in.hid_out (the attention sublayer's output).
+template <int R>
+static __device__ void stage_rows_sums(const ProjArgs &a, int16_t *xs, int rows, int tid) {
+    const int T = blockDim.x - 32, K = a.K;
+    const ArInput &in = a.in;
+    for (int i0 = 4 * tid; i0 < R * K; i0 += 4 * kStageBatch * T) {
+        longlong4 sv[kStageBatch];
+        uint2 rv[kStageBatch];
+#pragma unroll
+        for (int k = 0; k < kStageBatch; k++) {  // all loads of a batch in flight first
+            const int i = i0 + 4 * k * T;
+            if (i < R * K && i / K < rows) {
+                sv[k] = *reinterpret_cast<const longlong4 *>(in.sums + i);
+                rv[k] = *reinterpret_cast<const uint2 *>(in.resid + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kStageBatch; k++) {
+            const int i = i0 + 4 * k * T;
+            if (i >= R * K) break;
+            uint2 x = make_uint2(0, 0);
+            if (i / K < rows) {
+                const int32_t y0 = sat16(lo16(rv[k].x) + round_mac(sv[k].x));
+                const int32_t y1 = sat16(hi16(rv[k].x) + round_mac(sv[k].y));
+                const int32_t y2 = sat16(lo16(rv[k].y) + round_mac(sv[k].z));
+                const int32_t y3 = sat16(hi16(rv[k].y) + round_mac(sv[k].w));
+                x.x = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
+                x.y = ((uint32_t)y2 & 0xffffu) | ((uint32_t)y3 << 16);
+                if (blockIdx.x == 0) *reinterpret_cast<uint2 *>(in.hid_out + i) = x;
+            }
+            *reinterpret_cast<uint2 *>(xs + i) = x;
+        }
+    }
+    consumer_sync();
+}
+
 // In-place RMSNorm of rows already staged in shared memory (all-reduce input);
 // red / inv_rms_s: the staging prologue's reduction scratch.
 template <int R>
@@ -141,6 +180,11 @@ static __device__ void stage_rows(const ProjArgs &a, const Step &st, int16_t *xs
     __shared__ int64_t red[CW][kMaxRows];
     if (a.in.ar.n > 1) {  // tensor parallel: the previous projection's all-reduce, finished here
         stage_rows_allreduce<R>(a, st, xs, rows, tid);
+        if (a.norm != nullptr) norm_rows_smem<R>(a, xs, rows, tid, red, inv_rms_s);
+        return;
+    }
+    if (a.in.sums != nullptr) {  // the fused attention's O sums, finished here
+        stage_rows_sums<R>(a, xs, rows, tid);
         if (a.norm != nullptr) norm_rows_smem<R>(a, xs, rows, tid, red, inv_rms_s);
         return;
     }
@@ -316,6 +360,9 @@ __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a
     const Step st = load_step(a.step);
     pdl_wait();
     pdl_trigger();
+    if (a.zero != nullptr)  // the previous kernel has read these sums: clear them for their next use
+        for (int i = blockIdx.x * (blockDim.x - 32) + tid; i < a.zero_n; i += gridDim.x * (blockDim.x - 32))
+            a.zero[i] = 0;
     const int rows = st.rows - a.row0;  // rows of this launch (a block may be split in row groups)
     const uint32_t ar_n = st.ar_base + a.ar_off;  // EPI_PARTIAL: this projection's all-reduce
     stage_rows<R>(a, st, xs, rows, tid);

@@ -70,8 +70,10 @@ __global__ void k_round_resid(const ResidArgs a) {
     pdl_wait();
     pdl_trigger();
     const int total = rows * a.n;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         a.out[i] = (int16_t)sat16((int32_t)a.resid[i] + round_mac(a.partial[i]));
+        if (a.clear != nullptr) a.clear[i] = 0;
+    }
 }
 
 // Peer all-reduce, receiving side, as a kernel of its own (single coarse

@@ -73,6 +73,9 @@ struct ArInput {
     uint32_t ar_off;     // all-reduce number = step->ar_base + ar_off
     const int16_t *resid;
     int16_t *hid_out;
+    // single GPU: the exact O sums [kMaxRows][K] the attention kernel added up
+    // (attention with the O projection fused); x = sat16(resid + round(sum))
+    const int64_t *sums;
 };
 
 struct ProjArgs {
@@ -105,6 +108,10 @@ struct ProjArgs {
     uint32_t ar_off;     // EPI_PARTIAL: all-reduce number = step->ar_base + ar_off
     ArInput in;          // activation rows from a peer all-reduce (in.ar.n > 1) instead of x
     int row0;            // first row of this launch (x / out / resid already offset)
+    // words [0, zero_n) of zero are cleared once the previous kernel has finished
+    // (the fused attention's O sums, read by that kernel's prologue)
+    int64_t *zero;
+    int zero_n;
 };
 
 // Tensor-core projection of blocks of 3..8 rows (mma_proj.cu): weights in
@@ -177,6 +184,15 @@ struct AttnArgs {
     unsigned long long pf_per_tile;
     int pf_late;         // issue it after the first cluster barrier (K and V in shared memory)
     int *error;          // device word: nonzero after a bounded wait expired
+    // O projection fused (k_attn, one row): o_w = the layer's O weights, head-major
+    // in the pair layout (head lh, O row j: hd/2 words at o_w + (lh*hidden + j)*hd/2),
+    // o_rows = O rows per CTA (hidden / cluster); each cluster adds its head's
+    // exact int64 partial of every O row into o_acc[row][hidden].
+    // o_w == nullptr: the head output goes to out.
+    const uint32_t *o_w;
+    int o_rows;
+    int hidden;
+    int64_t *o_acc;
 };
 
 struct NormArgs {
@@ -195,6 +211,7 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
     int16_t *out;
     int n;
     const Step *step;
+    int64_t *clear;      // non-null (== partial): each sum is cleared once read (the fused O sums)
 };
 
 // Per-operator (feature) kernels, feature.cu.  Slot orders of the packed
@@ -243,7 +260,7 @@ cudaError_t attn_configure(int max_smem_bytes, int cluster);
 cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s);
 cudaError_t attn_rows_configure(int max_smem_bytes, int cluster);
 size_t attn_rows_smem_bytes(int tpc, int cluster);
-size_t attn_smem_bytes(int tpc, int hd, int cluster);
+size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 cudaError_t proj_configure(int max_smem_bytes);

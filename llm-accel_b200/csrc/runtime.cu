@@ -93,6 +93,13 @@ struct llmx_ctx {
     int16_t *hid[3] = {nullptr, nullptr, nullptr};
     int16_t *q = nullptr, *att = nullptr, *act = nullptr;
     int64_t *partial = nullptr;
+    // one-row attention with the O projection fused (single GPU, LLMX_ATTN_FUSE_O):
+    // the exact O sums [kMaxRows][hidden], finished by the next kernel's prologue
+    bool fuse_o = true;
+    int64_t *o_acc = nullptr;
+    // the O weights once more, head-major ([head][hidden rows][hd/2] words per
+    // layer), so that a fused-attention CTA's slice is one contiguous copy
+    uint32_t *o_heads = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
@@ -212,7 +219,7 @@ int allreduce_resid(llmx_ctx *c, uint32_t rows, uint32_t ar_off, int16_t *out, c
     }
     CKN(ncclAllReduce(c->partial, c->partial, (size_t)rows * c->s.hidden, ncclInt64, ncclSum, c->comm,
                       c->stream));
-    ResidArgs r{c->partial, resid, out, c->s.hidden, c->step};
+    ResidArgs r{c->partial, resid, out, c->s.hidden, c->step, nullptr};
     CK(launch_round_resid(r, (int)rows, c->stream));
     c->launches += 1;
     return LLMX_OK;
@@ -272,6 +279,12 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
 // attn_rows_min rows one cluster per head covering every row.
 cudaError_t launch_attention(llmx_ctx *c, AttnArgs t, uint32_t rows);
 
+// One-row attention with the O projection fused: single GPU, the per-(row, head)
+// kernel, and Gate/Up + Down on the dp2a kernel (whose prologue / clearing
+// finish the sums).
+bool use_fuse_o(const llmx_ctx *c, uint32_t rows);
+void set_fuse_o(llmx_ctx *c, AttnArgs &t, uint32_t layer);
+
 // Cluster size of an attention launch of `rows` rows.
 void pick_attn_cluster(const llmx_ctx *c, AttnArgs &t, uint32_t rows) {
     if (c->attn_wide && c->attn_wide_div * (int)rows * c->hq * kClusterWide <= c->nsm) {
@@ -290,6 +303,7 @@ cudaError_t launch_attention(llmx_ctx *c, AttnArgs t, uint32_t rows) {
         return launch_attn_rows(t, c->stream);
     }
     pick_attn_cluster(c, t, rows);
+    if (t.o_w != nullptr) t.o_rows = t.hidden / t.cluster;  // O rows per CTA of the chosen cluster
     if (rows > (uint32_t)c->attn_pf_rows) t.pf_per_tile = 0;
     return launch_attn(t, (int)rows, c->stream);
 }
@@ -347,24 +361,57 @@ bool use_mma(const llmx_ctx *c, uint32_t rows, int proj) {
     return c->mma && (int)rows >= c->mma_min_rows && ((c->mma_proj >> proj) & 1);
 }
 
-// A peer all-reduce whose finishing step is still to come: its number within
-// the call, the residual to add and where the finished rows belong.
+bool use_fuse_o(const llmx_ctx *c, uint32_t rows) {
+    return c->fuse_o && c->size == 1 && rows == 1 && (int)rows < c->attn_rows_min && c->s.hidden % kClusterWide == 0 &&
+           !use_mma(c, rows, MP_GU) &&
+           !use_mma(c, rows, MP_D);
+}
+
+void set_fuse_o(llmx_ctx *c, AttnArgs &t, uint32_t layer) {
+    t.o_w = c->o_heads + (size_t)layer * c->w_o;
+    t.o_rows = c->s.hidden / t.cluster;
+    t.hidden = c->s.hidden;
+    t.o_acc = c->o_acc;
+    // the L2 warm-up starts after the O weights, which this kernel reads itself
+    const unsigned long long o_bytes = c->w_o * 4ull;
+    t.pf += o_bytes;
+    t.pf_bytes = t.pf_bytes > o_bytes ? t.pf_bytes - o_bytes : 0;
+}
+
+
+// Exact sums whose rounding (+ residual) is still to come: a peer all-reduce
+// (its number within the call), or the fused attention's O sums (local); the
+// residual to add and where the finished rows belong.
 struct PendingAr {
     bool active = false;
+    bool local = false;
     uint32_t off = 0;
     const int16_t *resid = nullptr;
     int16_t *out = nullptr;
 };
 
-// Route a projection's activation input through a pending peer all-reduce
-// (the projection's prologue finishes it).
+// Route a projection's activation input through pending sums (the projection's
+// prologue finishes them).
 void take_input(llmx_ctx *c, ProjArgs &a, PendingAr &pend) {
     if (!pend.active) return;
-    a.in.ar = c->ar;
-    a.in.ar_off = pend.off;
+    if (pend.local) {
+        a.in.sums = c->o_acc;
+    } else {
+        a.in.ar = c->ar;
+        a.in.ar_off = pend.off;
+    }
     a.in.resid = pend.resid;
     a.in.hid_out = pend.out;
-    pend.active = false;
+    pend.active = pend.local = false;
+}
+
+// The fused attention's O sums as a kernel of their own: round, + residual,
+// clear the sums.
+int finish_o_sums(llmx_ctx *c, uint32_t rows, int16_t *out, const int16_t *resid) {
+    ResidArgs r{c->o_acc, resid, out, c->s.hidden, c->step, c->o_acc};
+    CK(launch_round_resid(r, (int)rows, c->stream));
+    c->launches += 1;
+    return LLMX_OK;
 }
 
 // After a tensor-parallel O / Down projection: leave the all-reduce pending for
@@ -450,7 +497,20 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
             set_stages(c, a, EPI_QKV, rt);
             CK(launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream));
         }
-        CK(launch_attention(c, attn_args(c, layer), rows));
+        AttnArgs t = attn_args(c, layer);
+        if (use_fuse_o(c, rows)) {  // O inside attention; the next prologue (or a finisher) rounds
+            set_fuse_o(c, t, layer);
+            CK(launch_attention(c, t, rows));
+            c->launches += 2;
+            if (fuse) {
+                pend.active = pend.local = true;
+                pend.resid = in;
+                pend.out = out;
+                return LLMX_OK;
+            }
+            return finish_o_sums(c, rows, out, in);
+        }
+        CK(launch_attention(c, t, rows));
         ProjArgs o = o_args(c, layer, out, in);
         o.ar_off = ar_next;
         if (use_mma(c, rows, MP_O)) {
@@ -469,6 +529,10 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         take_input(c, g, pend);
         ProjArgs d = down_args(c, layer, out, in);
         d.ar_off = ar_next;
+        if (g.in.sums != nullptr) {  // Gate/Up finished the fused O sums: Down clears them
+            d.zero = c->o_acc;
+            d.zero_n = (int)rows * s.hidden;
+        }
         if (use_mma(c, rows, MP_GU)) {
             const int rc = launch_mma(c, g, MP_GU, layer, EPI_SILU);
             if (rc) return rc;
@@ -532,6 +596,8 @@ int check_device_error(llmx_ctx *c) {
     CK(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (v != 0) {
         CK(cudaMemset(c->err, 0, sizeof(int)));
+        // a call that stopped part-way may leave fused-O sums behind
+        CK(cudaMemset(c->o_acc, 0, sizeof(int64_t) * kMaxRows * c->s.hidden));
         if (v == kErrTokenRange) {
             g_last_error = "a token id reached the embedding gather outside the vocabulary";
             return LLMX_ERR_RANGE;
@@ -563,7 +629,8 @@ int enqueue_stack(llmx_ctx *c, uint32_t rows, uint32_t layer_begin, uint32_t lay
         if (rc) return rc;
     }
     if (pend.active) {
-        const int rc = allreduce_resid(c, rows, pend.off, pend.out, pend.resid);
+        const int rc = pend.local ? finish_o_sums(c, rows, pend.out, pend.resid)
+                                  : allreduce_resid(c, rows, pend.off, pend.out, pend.resid);
         if (rc) return rc;
     }
     if (final_norm) return enqueue_task(c, LLMX_OP_FINAL_NORM, 0, rows, 1, 0, ar_next, false, pend);
@@ -728,6 +795,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
+    c->fuse_o = env_int("LLMX_ATTN_FUSE_O", 1, 0, 1) == 1 && c->size == 1;
     auto bail = [&](int code) {
         release(c);
         return code;
@@ -742,7 +810,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
     e = proj_configure(kProjSmem);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
-    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster), kCluster);
+    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster, s.hidden / kCluster), kCluster);
     if (e == cudaSuccess) e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
     c->attn_rows_min = env_int("LLMX_ATTN_ROWS_MIN", 2, 2, 9);
@@ -755,7 +823,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_wide_div = env_int("LLMX_ATTN_WIDE_DIV", 1, 1, 8);
     if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && c->attn_wide_div * c->hq * kClusterWide <= c->nsm &&
         env_int("LLMX_ATTN_WIDE", 1, 0, 1) == 1) {
-        e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide), kClusterWide);
+        e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide, s.hidden / kClusterWide),
+                           kClusterWide);
         if (e == cudaSuccess)
             e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max_wide, kClusterWide), kClusterWide);
         if (e == cudaSuccess) c->attn_wide = true;
@@ -782,8 +851,15 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->q, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->att, kMaxRows * (size_t)c->Hq)) ||
         (rc = dalloc(c, &c->act, kMaxRows * (size_t)c->Il)) || (rc = dalloc(c, &c->partial, kMaxRows * H)) ||
+        (rc = dalloc(c, &c->o_acc, kMaxRows * H)) ||
         (rc = dalloc(c, &c->step, 1)) || (rc = dalloc(c, &c->err, 1)))
         return bail(rc);
+    // head-major O weights for the fused decode attention (w_o words per layer);
+    // without the memory the O projection stays a kernel of its own
+    if (c->fuse_o && dalloc(c, &c->o_heads, c->w_o * s.layers) != LLMX_OK) {
+        c->fuse_o = false;
+        (void)cudaGetLastError();
+    }
 
     // tensor-core projections for blocks of mma_min_rows..8 rows: QKV tiles are
     // heads, so head_dim must be 128 (every Qwen profile); LLMX_MMA=0 disables
@@ -911,6 +987,10 @@ int llmx_upload_layer(llmx_ctx *c, uint32_t layer, const int16_t *dense) {
     // Q,K,V are consecutive dense matrices with row length H
     CK(launch_pack_pairs(c->staging + off[0], H, 0, H, c->slot_qkv, c->Hq + 2 * c->KV, w, c->stream));
     CK(launch_pack_pairs(c->staging + off[3], H, c->h0 * c->hd, c->Hq, c->slot_o, H, w + c->w_qkv, c->stream));
+    if (c->o_heads)  // head h: its hd columns of every O row, rows contiguous
+        for (int h = 0; h < c->hq; h++)
+            CK(launch_pack_pairs(c->staging + off[3], H, (c->h0 + h) * c->hd, c->hd, c->slot_o, H,
+                                 c->o_heads + (size_t)layer * c->w_o + (size_t)h * H * (c->hd / 2), c->stream));
     CK(launch_pack_pairs(c->staging + off[4], H, 0, H, c->slot_gu, 2 * c->Il, w + c->w_qkv + c->w_o, c->stream));
     CK(launch_pack_pairs(c->staging + off[6], s.inter, c->c0, c->Il, c->slot_d, H,
                          w + c->w_qkv + c->w_o + c->w_gu, c->stream));
@@ -1253,7 +1333,11 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
             set_stages(c, a, EPI_QKV, rt);
             return launch_proj(a, EPI_QKV, rt, grid_for(c, a.npairs, rt, a.K), c->stream);
         }
-        case LLMX_KERNEL_ATTN: return launch_attention(c, attn_args(c, layer), rows);
+        case LLMX_KERNEL_ATTN: {  // as a stack launches it (with the O projection when fused)
+            AttnArgs t = attn_args(c, layer);
+            if (use_fuse_o(c, rows)) set_fuse_o(c, t, layer);
+            return launch_attention(c, t, rows);
+        }
         case LLMX_KERNEL_O: {
             ProjArgs o = o_args(c, layer, out, in);
             o.ar.n = 0;  // timing only: keep the partial sums local, signal no rank
@@ -1291,6 +1375,9 @@ int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position,
     if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+    // repeated fused-attention launches accumulate into the O sums: clear them
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->o_acc, 0, sizeof(int64_t) * kMaxRows * c->s.hidden, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return fail_cuda(e, "llmx_time_kernel");
     *ms_per_launch = (double)ms / iters;
     return LLMX_OK;
@@ -1319,6 +1406,8 @@ int llmx_selftest_ar_timeout(llmx_ctx *c, uint32_t poll_limit) {
     CK(cudaStreamSynchronize(c->stream));
     return check_device_error(c);
 }
+
+int llmx_decode_fuses_o(const llmx_ctx *c) { return c && use_fuse_o(c, 1) ? 1 : 0; }
 
 int llmx_allreduce_kind(const llmx_ctx *c) {
     if (!c) return -1;

@@ -137,6 +137,7 @@ def lib():
             "llmx_lm_head_argmax_device": (C.c_int, [vp, C.c_uint32, C.c_uint32, vp, C.c_uint32, vp, vp]),
             "llmx_upload_vocab": (C.c_int, [vp, vp]),
             "llmx_allreduce_kind": (C.c_int, [vp]),
+            "llmx_decode_fuses_o": (C.c_int, [vp]),
             "llmx_selftest_ar_timeout": (C.c_int, [vp, C.c_uint32]),
             "llmx_generate": (C.c_int, [vp, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp]),
         }
@@ -441,6 +442,11 @@ class Accelerator:
     def selftest_ar_timeout(self, poll_limit):
         """Return code of a bounded all-reduce wait that is made to expire (LLMX_ERR_TIMEOUT)."""
         return lib().llmx_selftest_ar_timeout(self.h, poll_limit)
+
+    @property
+    def decode_fuses_o(self):
+        """Whether one-row stacks run the O projection inside the attention kernel."""
+        return bool(lib().llmx_decode_fuses_o(self.h))
 
     @property
     def allreduce_kind(self):
