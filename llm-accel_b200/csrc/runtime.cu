@@ -821,8 +821,12 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     }
     // LLMX_ATTN_WIDE=0 keeps 8-CTA clusters everywhere
     c->attn_wide_div = env_int("LLMX_ATTN_WIDE_DIV", 1, 1, 8);
+    // LLMX_ATTN_WIDE=2: 16-CTA clusters whatever the head count (every one-row
+    // attention launch; several CTAs then share an SM)
+    const int wide_env = env_int("LLMX_ATTN_WIDE", 1, 0, 2);
+    if (wide_env == 2) c->attn_wide_div = 0;
     if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && c->attn_wide_div * c->hq * kClusterWide <= c->nsm &&
-        env_int("LLMX_ATTN_WIDE", 1, 0, 1) == 1) {
+        wide_env >= 1) {
         e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide, s.hidden / kClusterWide),
                            kClusterWide);
         if (e == cudaSuccess)
