@@ -35,6 +35,7 @@ def main():
     ap.add_argument("--max-seq", type=int, default=2304)
     ap.add_argument("--table", action="store_true")
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--stack", action="store_true", help="decode steps through llmx_stack (one CUDA graph each)")
     ap.add_argument("--rows", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--iters", type=int, default=40)
@@ -68,6 +69,12 @@ def main():
         for rows in (1, 8):
             out[f"rows{rows}"] = {n: acc.time_kernel(i, 0, P, rows, args.iters) * 1e3 for i, n in enumerate(NAMES)}
         print(json.dumps({"position": P, "layers": s.layers, "us_per_launch": out}, indent=1))
+    if args.stack:
+        hs = m.embed(rng.integers(0, s.vocab, 8 * args.steps))
+        for step in range(args.steps):
+            pos = P + step * args.rows
+            acc.stack(hs[step * args.rows:(step + 1) * args.rows], position=pos)
+        print("stack steps done")
     if args.eager:
         for step in range(args.steps):
             pos = P + step * args.rows
