@@ -112,20 +112,35 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
         if (a.inv_elems == 0) {
             if (tid < kMaxRows) inv_s[tid] = a.inv_rms_const;
         } else {  // general RMSNorm: full-row sums of squares (stream_rmsnorm compute_stream.cpp:242-283)
-            for (int r = 0; r < kMaxRows; r++) {
+            // T / 8 threads per row, 16-byte loads, four in flight per thread: every
+            // row's sum in one pass (the rows are independent)
+            if (tid < kMaxRows) red[tid] = 0;
+            named_sync(2, T);
+            const int tpr = T / kMaxRows, r = tid / tpr, sub = tid - r * tpr;
+            if (r < rows) {
+                const uint4 *x4 = reinterpret_cast<const uint4 *>(a.x + (size_t)r * K);
+                const int KV8 = K >> 3;
                 int64_t part = 0;
-                if (r < rows)
-                    for (int i = tid; i < K; i += T) {
-                        const int32_t v = a.x[(size_t)r * K + i];
-                        part += (int64_t)v * v;
+                for (int v0 = sub; v0 < KV8; v0 += 4 * tpr) {
+                    uint4 q[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int v = v0 + k * tpr;
+                        q[k] = v < KV8 ? x4[v] : make_uint4(0, 0, 0, 0);
                     }
-                for (int o = 16; o >= 1; o >>= 1) part += shfl_xor64(part, o);
-                if ((tid & 31) == 0) red[r * 8 + (tid >> 5)] = part;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t w[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            part += (int64_t)lo16(w[i]) * lo16(w[i]) + (int64_t)hi16(w[i]) * hi16(w[i]);
+                    }
+                }
+                atomicAdd(reinterpret_cast<unsigned long long *>(red + r), (unsigned long long)part);
             }
             named_sync(2, T);
             if (tid < kMaxRows) {
-                int64_t sum = 0;
-                for (int w = 0; w < T / 32; w++) sum += red[tid * 8 + w];
+                const int64_t sum = red[tid];
                 inv_s[tid] = inv_rms_q88(sum > INT32_MAX ? INT32_MAX : (int32_t)sum, a.inv_elems);
             }
         }
