@@ -145,6 +145,7 @@ struct MmaArgs {
     int stages;          // ring stages of kMmaItemBytes
     int max_items;       // items of the largest CTA range (activation slots)
     int *error;
+    const int32_t *wsum; // [T][C+1][128] prefix over chunks of each tile row's weight sums (k_mma_wsum)
 };
 cudaError_t launch_mma_proj(const MmaArgs &a, int epi, int grid, cudaStream_t s);
 cudaError_t mma_configure(int max_smem_bytes);
@@ -152,6 +153,8 @@ size_t mma_smem_bytes(int stages, int max_items);
 int mma_stages(int max_items, int max_smem);
 cudaError_t launch_pack_mma(const int16_t *dense, int ld, int col0, int K, int C, const int32_t *rows_of, int T,
                             uint8_t *dst, cudaStream_t s);
+cudaError_t launch_mma_wsum(const int16_t *dense, int ld, int col0, int K, int C, const int32_t *rows_of, int T,
+                            int32_t *wsum, cudaStream_t s);
 
 // CTAs per (row, query head) attention cluster: 8, or 16 (a non-portable size
 // B200 supports) when few heads leave most SMs idle, so that the contexts

@@ -6,16 +6,20 @@
 // 138-205; kernel/compute_core_8x64_unified.cpp:10-39; golden_projection
 // host/host_qwen_8x64.cpp:3105-3142).
 //
-// Exactness.  Split every int16 into a signed high byte and an unsigned low
-// byte, w = 256*wh + wl and x = 256*xh + xl.  Then
-//   sum w*x = 65536*sum(wh*xh) + 256*(sum(wh*xl) + sum(wl*xh)) + sum(wl*xl)
-// and each of the four byte sums is an int8 (s8/u8) tensor-core contraction
-// with an int32 accumulator that cannot overflow for K <= 11008:
-// |wh*xh| <= 2^14, |wh*xl| <= 128*255, wl*xl <= 255^2 = 65025 and
-// 65025 * 11008 < 2^31.  The four int32 sums are recombined in int64 by the
-// epilogue, so the result is the exact int64 dot product, as in the golden
-// model -- the operand widths of the reference fit the tensor cores exactly
-// once split into bytes.
+// Exactness.  Split every weight into a signed high byte and an unsigned low
+// byte, w = 256*wh + wl, and every activation into a signed high byte and a
+// signed low byte, x = 256*xh + xs + 128 with xs = (x & 255) - 128.  Then
+//   sum w*x = 65536*sum(wh*xh) + 256*(sum(wh*xs) + sum(wl*xh)) + sum(wl*xs)
+//             + 128*sum(w)
+// Because xh and xs are both signed, the B operand [xh rows | xs rows] is one
+// s8 matrix of N = 16 rows, and each weight plane needs one MMA per K-step:
+// wh x B (s8 x s8) and wl x B (u8 x s8).  The int32 accumulators cannot
+// overflow for K <= 11008 (|wh*xh|, |wh*xs| <= 2^14, |wl*xh|, |wl*xs| <=
+// 255*128; 32640 * 11008 < 2^31).  sum(w) over the chunks a CTA accumulated
+// comes from a per-tile-row prefix table of weight sums built at upload
+// (k_mma_wsum).  The epilogue recombines in int64, so the result is the exact
+// int64 dot product, as in the golden model -- the operand widths of the
+// reference fit the tensor cores exactly once split into bytes.
 //
 // B200 mapping.  Weights are re-laid out at upload into "items": one item is
 // one tile of 128 output rows x 128 inputs, as two 16 KiB byte planes (high,
@@ -24,8 +28,8 @@
 // into a shared-memory ring stage.  A projection is T tiles x C chunks of K;
 // the T*C items are split evenly and contiguously over the CTAs (stream-K), so
 // every CTA streams one contiguous byte range.  Per item the MMA thread issues
-// 4 K-steps x 4 byte-plane products (M = 128, N = 8 activation rows, K = 32
-// bytes) into one of two 32-column TMEM accumulator sets; four epilogue warps
+// 4 K-steps x 2 weight-plane products (M = 128, N = 16 = 8 activation rows x 2
+// byte planes, K = 32 bytes) into one of two 32-column TMEM accumulator sets; four epilogue warps
 // read the sums with tcgen05.ld (one TMEM lane = one output row) and run the
 // fused epilogue of the path (RoPE + KV append, SiLU x up, residual, or the
 // tensor-parallel partial sums).  A tile shared by two or more CTAs is
@@ -41,7 +45,7 @@
 namespace llmx {
 
 constexpr int kMmaThreads = 6 * 32;  // warp 0: TMEM + MMA issue, warp 1: weight producer, warps 2-5: epilogue
-constexpr int kTmemCols = 64;        // two accumulator sets x {hh, hl, lh, ll} x 8 rows
+constexpr int kTmemCols = 64;        // two accumulator sets x {wh x [xh|xs], wl x [xh|xs]} x 8 rows
 constexpr int kMmaHdr = 1024;        // barriers and flags at the start of dynamic shared memory
 constexpr int kMmaMaxStages = 8;
 
@@ -54,9 +58,10 @@ static __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lb
            (1ull << 46);
 }
 // Instruction descriptor, kind::i8: int32 accumulator, A and B K-major,
-// M = 128, N = 8; a_signed / b_signed select s8 (1) or u8 (0).
+// M = 128, N = 16; a_signed / b_signed select s8 (1) or u8 (0).
 static __host__ __device__ constexpr uint32_t umma_idesc_i8(int a_signed, int b_signed) {
-    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
+    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((16u >> 3) << 17) |
+           ((128u >> 4) << 24);
 }
 static __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -185,11 +190,12 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
                         xw[q] = ((uint32_t)y0 & 0xffffu) | ((uint32_t)y1 << 16);
                     }
                 }
-                // bytes of 4 consecutive int16 (two words): high bytes 1,3,5,7 and low bytes 0,2,4,6
+                // bytes of 4 consecutive int16 (two words): high bytes 1,3,5,7 and low
+                // bytes 0,2,4,6, the low bytes stored as signed (x & 255) - 128
                 hw[2 * h] = __byte_perm(xw[0], xw[1], 0x7531);
-                lw[2 * h] = __byte_perm(xw[0], xw[1], 0x6420);
+                lw[2 * h] = __byte_perm(xw[0], xw[1], 0x6420) ^ 0x80808080u;
                 hw[2 * h + 1] = __byte_perm(xw[2], xw[3], 0x7531);
-                lw[2 * h + 1] = __byte_perm(xw[2], xw[3], 0x6420);
+                lw[2 * h + 1] = __byte_perm(xw[2], xw[3], 0x6420) ^ 0x80808080u;
             }
             char *slot = bsl + (size_t)j * 2048 + kc * 128 + r * 16;
             *reinterpret_cast<uint4 *>(slot) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -368,8 +374,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
 
         if (warp == 0) {  // ---------------- MMA issue (one thread) ----------------------
             if (lane == 0) {
-                constexpr uint32_t kSS = umma_idesc_i8(1, 1), kSU = umma_idesc_i8(1, 0), kUS = umma_idesc_i8(0, 1),
-                                   kUU = umma_idesc_i8(0, 0);
+                constexpr uint32_t kSS = umma_idesc_i8(1, 1), kUS = umma_idesc_i8(0, 1);
                 int tiles_done = 0;
                 bool ok = true;
                 for (int j = 0; j < n && ok; j++) {
@@ -381,17 +386,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t ah = smem_u32(ring + (size_t)(j % S) * kMmaItemBytes), al = ah + 16384;
-                    const uint32_t bh = smem_u32(bsl + (size_t)j * 2048), bl = bh + 1024;
+                    // B: the slot's high plane (rows 0-7) and signed low plane (rows 8-15),
+                    // one 8-row core-matrix group apart (SBO 1024): one N = 16 operand
+                    const uint32_t bh = smem_u32(bsl + (size_t)j * 2048);
                     const uint32_t d = tmem + (uint32_t)b * 32;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {  // 32-byte K-steps of the 128-byte chunk
                         const uint32_t acc = (first && k == 0) ? 0u : 1u;
                         const uint64_t dah = umma_desc(ah + k * 256, 128, 1024), dal = umma_desc(al + k * 256, 128, 1024);
-                        const uint64_t dbh = umma_desc(bh + k * 256, 128, 1024), dbl = umma_desc(bl + k * 256, 128, 1024);
-                        umma_i8(d + 0, dah, dbh, kSS, acc);
-                        umma_i8(d + 8, dah, dbl, kSU, acc);
-                        umma_i8(d + 16, dal, dbh, kUS, acc);
-                        umma_i8(d + 24, dal, dbl, kUU, acc);
+                        const uint64_t db = umma_desc(bh + k * 256, 128, 1024);
+                        umma_i8(d + 0, dah, db, kSS, acc);   // columns 0-7 wh.xh, 8-15 wh.xs
+                        umma_i8(d + 16, dal, db, kUS, acc);  // columns 16-23 wl.xh, 24-31 wl.xs
                     }
                     umma_commit(empty + j % S);  // ring stage free once these MMAs are done
                     if (last) {
@@ -424,12 +429,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)b * 32, v);
                 tc_fence_before();
                 mbar_arrive(tempty + b);
+                const int seg0 = max(w0, t * a.C), seg1 = min(w1, (t + 1) * a.C);
+                // + 128 * (sum of this tile row's weights over the chunks accumulated here)
+                const int32_t *ws = a.wsum + (size_t)t * (a.C + 1) * 128 + m;
+                const int64_t corr =
+                    128 * (int64_t)(ws[(size_t)(seg1 - t * a.C) * 128] - ws[(size_t)(seg0 - t * a.C) * 128]);
                 int64_t Sm[kMaxRows];
 #pragma unroll
                 for (int r = 0; r < kMaxRows; r++)
                     Sm[r] = (int64_t)(int32_t)v[r] * 65536 +
-                            ((int64_t)(int32_t)v[8 + r] + (int64_t)(int32_t)v[16 + r]) * 256 + (int64_t)(int32_t)v[24 + r];
-                const int seg0 = max(w0, t * a.C), seg1 = min(w1, (t + 1) * a.C);
+                            ((int64_t)(int32_t)v[8 + r] + (int64_t)(int32_t)v[16 + r]) * 256 + (int64_t)(int32_t)v[24 + r] +
+                            corr;
                 if (seg0 != t * a.C || seg1 != (t + 1) * a.C) {
                     // shared tile: leave the partial sums, count in; the last CTA finishes it
                     const int which = t == t0 ? 0 : 1;
@@ -560,6 +570,28 @@ cudaError_t launch_pack_mma(const int16_t *dense, int ld, int col0, int K, int C
     const size_t groups = (size_t)T * C * 2 * 128 * 8;
     int blocks = (int)std::min<size_t>((groups + 255) / 256, 65535 * 8);
     k_pack_mma<<<blocks, 256, 0, s>>>(dense, ld, col0, K, C, rows_of, T, dst);
+    return cudaGetLastError();
+}
+
+// Prefix over K-chunks of every tile row's weight sums: wsum[(t*(C+1) + c)*128 + m]
+// = sum of the row's weights in chunks [0, c) (|value| < 2^29 for K <= 11008).
+__global__ void k_mma_wsum(const int16_t *__restrict__ dense, int ld, int col0, int K, int C,
+                           const int32_t *__restrict__ rows_of, int T, int32_t *__restrict__ wsum) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;  // tile row t*128 + m
+    if (i >= T * 128) return;
+    const int t = i >> 7, m = i & 127, row = rows_of[i];
+    int32_t acc = 0;
+    wsum[(size_t)t * (C + 1) * 128 + m] = 0;
+    for (int c = 0; c < C; c++) {
+        if (row >= 0)
+            for (int k = c * 128; k < min(K, (c + 1) * 128); k++) acc += dense[(size_t)row * ld + col0 + k];
+        wsum[((size_t)t * (C + 1) + c + 1) * 128 + m] = acc;
+    }
+}
+
+cudaError_t launch_mma_wsum(const int16_t *dense, int ld, int col0, int K, int C, const int32_t *rows_of, int T,
+                            int32_t *wsum, cudaStream_t s) {
+    k_mma_wsum<<<(T * 128 + 127) / 128, 128, 0, s>>>(dense, ld, col0, K, C, rows_of, T, wsum);
     return cudaGetLastError();
 }
 

@@ -62,6 +62,7 @@ void llmx::set_last_error(const std::string &msg) { g_last_error = msg; }
 struct MmaGeom {
     int T = 0, C = 0, K = 0, n_out = 0;
     size_t offset = 0;  // bytes from the start of the layer's item blob
+    size_t wsum_offset = 0;  // int32 entries from the start of the layer's weight-sum tables (T*(C+1)*128)
     size_t items() const { return (size_t)T * C; }
 };
 
@@ -136,6 +137,8 @@ struct llmx_ctx {
     MmaGeom mg[4]{};             // QKV, O, Gate/Up, Down of this rank
     size_t mma_layer_bytes = 0;
     uint8_t *mbuf = nullptr;
+    int32_t *mma_wsum = nullptr;  // per layer: the projections' weight-sum prefix tables
+    size_t mma_wsum_layer = 0;    // int32 entries per layer
     int64_t *mma_scratch = nullptr;
     int *mma_cnt = nullptr;
     int32_t *mma_rows[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -460,6 +463,7 @@ int launch_mma(llmx_ctx *c, const ProjArgs &p, int proj, uint32_t layer, int epi
     m.scratch = c->mma_scratch;
     m.tile_cnt = c->mma_cnt;
     m.error = c->err;
+    m.wsum = c->mma_wsum + (size_t)layer * c->mma_wsum_layer + g.wsum_offset;
     const int items = (int)g.items();
     const int grid = std::min(c->nsm, items);
     m.max_items = (items + grid - 1) / grid;
@@ -878,15 +882,18 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         g[MP_O].T = cdiv(Hi, 128), g[MP_O].C = cdiv(c->Hq, 128), g[MP_O].K = c->Hq, g[MP_O].n_out = Hi;
         g[MP_GU].T = cdiv(c->Il, 64), g[MP_GU].C = cdiv(Hi, 128), g[MP_GU].K = Hi, g[MP_GU].n_out = c->Il;
         g[MP_D].T = cdiv(Hi, 128), g[MP_D].C = cdiv(c->Il, 128), g[MP_D].K = c->Il, g[MP_D].n_out = Hi;
-        size_t off = 0;
+        size_t off = 0, woff = 0;
         int tmax = 0;
         for (int p = 0; p < 4; p++) {
             g[p].offset = off;
             off += g[p].items() * kMmaItemBytes;
+            g[p].wsum_offset = woff;
+            woff += (size_t)g[p].T * (g[p].C + 1) * 128;
             tmax = std::max(tmax, g[p].T);
         }
         c->mma_layer_bytes = off;
-        if ((rc = dalloc(c, &c->mbuf, off * s.layers)) ||
+        c->mma_wsum_layer = woff;
+        if ((rc = dalloc(c, &c->mbuf, off * s.layers)) || (rc = dalloc(c, &c->mma_wsum, woff * s.layers)) ||
             (rc = dalloc(c, &c->mma_scratch, (size_t)c->nsm * 2 * kMaxRows * 128)) ||
             (rc = dalloc(c, &c->mma_cnt, (size_t)tmax)))
             return bail(rc);
@@ -1009,6 +1016,16 @@ int llmx_upload_layer(llmx_ctx *c, uint32_t layer, const int16_t *dense) {
                            mb + g[MP_GU].offset, c->stream));
         CK(launch_pack_mma(c->staging + off[6], s.inter, c->c0, c->Il, g[MP_D].C, c->mma_rows[MP_D], g[MP_D].T,
                            mb + g[MP_D].offset, c->stream));
+        // weight-sum prefix tables (the signed low activation bytes' correction)
+        int32_t *ws = c->mma_wsum + (size_t)layer * c->mma_wsum_layer;
+        CK(launch_mma_wsum(c->staging + off[0], H, 0, H, g[MP_QKV].C, c->mma_rows[MP_QKV], g[MP_QKV].T,
+                           ws + g[MP_QKV].wsum_offset, c->stream));
+        CK(launch_mma_wsum(c->staging + off[3], H, c->h0 * c->hd, c->Hq, g[MP_O].C, c->mma_rows[MP_O], g[MP_O].T,
+                           ws + g[MP_O].wsum_offset, c->stream));
+        CK(launch_mma_wsum(c->staging + off[4], H, 0, H, g[MP_GU].C, c->mma_rows[MP_GU], g[MP_GU].T,
+                           ws + g[MP_GU].wsum_offset, c->stream));
+        CK(launch_mma_wsum(c->staging + off[6], s.inter, c->c0, c->Il, g[MP_D].C, c->mma_rows[MP_D], g[MP_D].T,
+                           ws + g[MP_D].wsum_offset, c->stream));
     }
     CK(cudaStreamSynchronize(c->stream));
     c->layer_loaded[layer] = true;
