@@ -150,8 +150,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         if (fuse_o) l2_prefetch_slice(reinterpret_cast<const char *>(ow_src), ow_bytes, 0, 1);
     }
     __syncthreads();
+    // the next kernel (Gate/Up or O) may launch -- and stream its weights on the
+    // SMs attention leaves free -- from the start when the context is long, or
+    // only once PV is done when it is short: its streaming then slows this
+    // kernel's latency-bound loads more than it gains (trigger_tiles, measured)
+    const bool early_trigger = st.position + r + 1 > a.trigger_tiles * kTile;
     pdl_wait();
-    pdl_trigger();
+    if (early_trigger) pdl_trigger();
     // every CTA of the cluster reaches every cluster barrier, also when it owns nothing
     const int ctx = st.position + r + 1;
     const int ntiles = row_ok ? (ctx + kTile - 1) / kTile : 0;
@@ -293,6 +298,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
     }
     cluster.sync();
+    if (!early_trigger) pdl_trigger();
     if (fuse_o && threadIdx.x == 0) {  // V is consumed: the buffer now receives the O slice
         mbar_expect_tx(m.bar + 2, ow_bytes);
         bulk_g2s(m.ow, ow_src, ow_bytes, m.bar + 2);

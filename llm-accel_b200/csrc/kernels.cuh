@@ -196,6 +196,8 @@ struct AttnArgs {
     int o_rows;
     int hidden;
     int64_t *o_acc;
+    int trigger_tiles;   // k_attn: let the next kernel launch at the start when the row's context exceeds
+                         // this many 64-position tiles, else once PV is done
 };
 
 struct NormArgs {

@@ -112,6 +112,10 @@ struct llmx_ctx {
     // slower); no gain at 8 rows.
     int attn_pf_tile_kb = 3584, attn_pf_kb = 72 * 1024, attn_pf_rows = 2;
     int attn_pf_late = 1;  // after attention's K/V loads (LLMX_ATTN_PREFETCH_LATE=0: at kernel start)
+    // one-row attention triggers the next kernel's launch at its start above this
+    // context (64-position tiles), else once PV is done (LLMX_ATTN_TRIGGER_TILES;
+    // measured: late +2.2 % at 9 tiles, early +2.2 % at 33)
+    int attn_trigger_tiles = 16;
     // peer all-reduce (tensor parallel): exchange regions of every rank (IPC-mapped)
     ArPeers ar{};
     char *ar_region = nullptr;
@@ -269,6 +273,7 @@ AttnArgs attn_args(llmx_ctx *c, uint32_t layer) {
     t.cluster = kCluster;
     t.qk_scale = c->qk_scale;
     t.error = c->err;
+    t.trigger_tiles = c->attn_trigger_tiles;
     // O then Gate/Up follow the QKV words of the layer blob
     t.pf = reinterpret_cast<const char *>(wl(c, layer) + c->w_qkv);
     t.pf_bytes = (c->w_o + c->w_gu) * 4ull;
@@ -796,6 +801,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 72 * 1024, 0, 1 << 22);
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
     c->attn_pf_late = env_int("LLMX_ATTN_PREFETCH_LATE", 1, 0, 1);
+    c->attn_trigger_tiles = env_int("LLMX_ATTN_TRIGGER_TILES", 16, 0, 1 << 20);
     c->gemv_ctas_per_sm = env_int("LLMX_GEMV_CTAS_PER_SM", 1, 1, 2);
     c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
