@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     const Step st = load_step(a.step);
     __syncthreads();
     pdl_wait();
-    pdl_trigger();
+    pdl_trigger();  // a block's next kernel may launch at once (a later trigger measured slower here)
     const int R = st.rows;
     const int ntiles = (st.position + R + kTile - 1) / kTile;  // the longest row's tiles
     const int tpc = max(1, (ntiles + C - 1) / C);
