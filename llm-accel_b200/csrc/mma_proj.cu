@@ -106,12 +106,8 @@ static __device__ __forceinline__ int cta_of_item(int i, int items, int grid) {
     return b;
 }
 
-// Activation rows -> the byte planes of every item chunk this CTA needs
-// (slot j = chunk of item w0 + j): RMS-normalised when a norm row is given.
-// Slot layout (2 KiB): high plane then low plane, each 8 rows x 128 bytes in
-// core-matrix order (16-byte column group kc at kc * 128, row r at r * 16).
-static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n, int rows, int tid, int T,
-                                      int32_t *inv_s, int64_t *red) {
+// RMSNorm factors of the activation rows (inv_s), when a norm row is given.
+static __device__ void mma_norm_rows(const MmaArgs &a, int rows, int tid, int T, int32_t *inv_s, int64_t *red) {
     const int K = a.K;
     if (a.norm != nullptr) {
         if (a.inv_elems == 0) {
@@ -151,11 +147,24 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
         }
         named_sync(2, T);
     }
+}
+
+// Activation rows -> the byte planes of every item chunk this CTA needs (slot j
+// = chunk of item w0 + j), RMS-normalised when a norm row is given, in item
+// order by the T threads of named barrier 4: after each round the count of
+// finished slots is published in *staged (release), so the MMA thread starts on
+// the first items while the later ones are still being staged.
+// Slot layout (2 KiB): high plane then low plane, each 8 rows x 128 bytes in
+// core-matrix order (16-byte column group kc at kc * 128, row r at r * 16).
+static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n, int rows, int tid, int T,
+                                      const int32_t *inv_s, int *staged) {
+    const int K = a.K;
     // one 16-element group (row r, column group kc of the chunk) per unit; the
     // loads of kBatch units are all in flight before any is used
     constexpr int kBatch = 4;
     const int units = n * kMaxRows * 8;
-    for (int u0 = tid; u0 < units; u0 += kBatch * T) {
+    for (int base = 0; base < units; base += kBatch * T) {
+        const int u0 = base + tid;
         uint4 xv[kBatch][2], wv[kBatch][2];
 #pragma unroll
         for (int k = 0; k < kBatch; k++) {
@@ -201,8 +210,19 @@ static __device__ void mma_stage_rows(const MmaArgs &a, char *bsl, int w0, int n
             *reinterpret_cast<uint4 *>(slot) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             *reinterpret_cast<uint4 *>(slot + 1024) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+        named_sync(4, T);
+        if (tid == 0) {
+            const int done = min(n, (base + kBatch * T) / (kMaxRows * 8));
+            asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(staged)), "r"(done) : "memory");
+        }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+}
+
+static __device__ __forceinline__ int ld_acquire_smem(const int *p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
 }
 
 // Final epilogue of one tile: thread m (TMEM lane) holds the exact sums of
@@ -301,6 +321,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
     int *last_s = reinterpret_cast<int *>(tmem_slot + 1);
     int *fail_s = last_s + 1;                              // [2][4] per-tile wait outcome of each epilogue warp
     int32_t *inv_s = fail_s + 8;                           // [8]
+    int *staged_s = reinterpret_cast<int *>(inv_s + 8);    // activation slots staged so far
     int64_t *red = reinterpret_cast<int64_t *>(smem + 512);  // [8][8]
     char *ring = smem + kMmaHdr;
     const int S = a.stages;
@@ -322,6 +343,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
             mbar_init(tempty + b, 128);  // every epilogue thread
         }
         mbar_init(done, 1);
+        *staged_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -369,8 +391,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
             for (int i = tid; i < 2049; i += 160) etab_s[i] = a.etab[i];
         pdl_wait();
         pdl_trigger();
-        mma_stage_rows(a, bsl, w0, n, st.rows, tid, 160, inv_s, red);
-        named_sync(1, 160);
+        mma_norm_rows(a, st.rows, tid, 160, inv_s, red);
 
         if (warp == 0) {  // ---------------- MMA issue (one thread) ----------------------
             if (lane == 0) {
@@ -383,6 +404,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
                     const int b = tiles_done & 1;
                     if (first && tiles_done >= 2 && !mbar_wait(tempty + b, ((tiles_done >> 1) - 1) & 1)) ok = false;
                     if (ok && !mbar_wait(full + j % S, (j / S) & 1)) ok = false;
+                    if (ok && ld_acquire_smem(staged_s) <= j) {  // this item's activation slot (bounded wait)
+                        ok = false;
+                        for (uint32_t it = 0; it < kSpinLimit; it++)
+                            if (ld_acquire_smem(staged_s) > j) {
+                                ok = true;
+                                break;
+                            }
+                    }
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t ah = smem_u32(ring + (size_t)(j % S) * kMmaItemBytes), al = ah + 16384;
@@ -410,7 +439,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
                 if (!mbar_wait(done, 0)) atomicExch(a.error, 2);
             }
             __syncwarp();
-        } else {  // ---------------- epilogue warps 2-5 -----------------------------------
+        } else {  // ---------------- epilogue warps 2-5: activation slots, then the tiles -------
+            mma_stage_rows(a, bsl, w0, n, st.rows, (int)threadIdx.x - 64, 128, inv_s, staged_s);
             const int q = warp & 3, m = q * 32 + lane;  // TMEM lane quarter of this warp, tile row
             const int t0 = w0 / a.C, t1 = n > 0 ? (w1 - 1) / a.C : t0 - 1;
             int tiles_done = 0;
