@@ -289,3 +289,45 @@ def test_attention_saturating_operands(llmx, oracle, rows):
     d = rng.integers(-2000, 2000, (1, s.hidden)).astype(np.int16)
     _assert_same(acc.stack(d, position=P + rows), ref.stack(d, P + rows), "decode after")
     acc.close()
+
+
+@pytest.mark.parametrize("env", [{}, {"LLMX_ATTN_FUSE_O": "0"}, {"LLMX_ATTN_TRIGGER_TILES": "0"}],
+                         ids=["o_fused", "o_kernel", "early_trigger"])
+def test_decode_attention_paths(llmx, oracle, monkeypatch, env):
+    """One-row decode runs the O projection inside the attention kernel (its
+    int64 sums finished by the Gate/Up prologue and cleared by Down); with
+    LLMX_ATTN_FUSE_O=0 the separate O kernel runs, and LLMX_ATTN_TRIGGER_TILES
+    moves the point where attention lets the next kernel launch.  Every variant
+    must match the oracle through a 3-layer stack of decode rows on both sides
+    of the 16-tile trigger threshold, and single Task 18 / 19 calls after it."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    s = llmx.shape("qwen-layer-long", layers=3)
+    m = llmx.Model(s).init_gaussian(20260719, 0.02)
+    acc = llmx.Accelerator(s)
+    try:
+        acc.upload_model(m)
+        assert acc.decode_fuses_o == (env.get("LLMX_ATTN_FUSE_O") != "0")
+        layers = [m.layer(l) for l in range(s.layers)]
+        ref = OracleState(oracle, oracle_shape(oracle, s), layers, m.norms())
+        rng = np.random.default_rng(11)
+        P = 1020
+        for l in range(s.layers):
+            k, v = random_kv(rng, s.kv_heads, P, s.head_dim)
+            acc.write_kv(l, 0, k, v)
+            ref.kc[l][:, :P] = k
+            ref.vc[l][:, :P] = v
+        for pos in range(P, P + 6):  # contexts 1021..1026: 16 tiles, then 17
+            d = m.embed([int(rng.integers(0, s.vocab))])
+            _assert_same(acc.stack(d, position=pos), ref.stack(d, pos), f"decode at {pos}")
+        h = m.embed([int(rng.integers(0, s.vocab))])  # the coarse tasks one by one
+        acc.write_hidden(1, h)
+        acc.bind(0, 1)
+        acc.task(llmx.OP_ATTENTION, 0, P + 6, 1)
+        want = ref.task18(0, h, P + 6)
+        _assert_same(acc.read_hidden(0, 1), want, "task 18")
+        acc.bind(1, 0)
+        acc.task(llmx.OP_FFN, 0, P + 6, 1)
+        _assert_same(acc.read_hidden(1, 1), ref.task19(0, want), "task 19")
+    finally:
+        acc.close()
