@@ -89,6 +89,14 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # nvidia-smi takes a while to start: the timed region begins only once it
+        # is sampling (bounded wait), so that the record covers the region
+        deadline = time.time() + 5.0
+        while self.proc is not None and time.time() < deadline and self.proc.poll() is None:
+            self.f.flush()
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
         self.t0 = time.time()
 
     def stop(self):

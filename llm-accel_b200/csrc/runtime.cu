@@ -103,7 +103,7 @@ struct llmx_ctx {
     uint32_t *o_heads = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
-    int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 96, gemv_ctas_per_sm = 1;
+    int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 160, gemv_ctas_per_sm = 1;
     int gemv_warps = 16;  // consumer warps of a projection CTA at most (LLMX_GEMV_WARPS)
     // L2 warm-up during attention of stacks of at most attn_pf_rows rows: attn_pf_tile_kb
     // KiB per 64-position context tile from the layer's O weights on, at most
@@ -796,7 +796,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->layer_loaded.assign(s.layers, false);
     c->ring_kb = env_int("LLMX_RING_KB", 96, 8, 220);
     c->ring_wide_kb = env_int("LLMX_RING_WIDE_KB", 176, 8, 200);  // measured best for Down on B200
-    c->ring_gu_kb = env_int("LLMX_RING_GU_KB", c->ring_kb, 8, 200);
+    c->ring_gu_kb = env_int("LLMX_RING_GU_KB", 160, 8, 200);  // 160: 685.9/672.7 -> 696.8/696.1 tok/s
     c->attn_pf_tile_kb = env_int("LLMX_ATTN_PREFETCH_TILE_KB", 3584, 0, 1 << 20);
     c->attn_pf_kb = env_int("LLMX_ATTN_PREFETCH_KB", 72 * 1024, 0, 1 << 22);
     c->attn_pf_rows = env_int("LLMX_ATTN_PREFETCH_ROWS", 2, 1, 8);
