@@ -37,12 +37,15 @@ extern "C" {
 #define LLMX_ERR_CUDA 100     /* a CUDA runtime call failed */
 #define LLMX_ERR_ARG 101      /* null pointer / size mismatch / bad buffer id */
 #define LLMX_ERR_STATE 102    /* model not loaded, context not ready */
-#define LLMX_ERR_NCCL 103     /* collective failed */
+#define LLMX_ERR_NCCL 103     /* collective failed (an asynchronous NCCL error aborts the communicator) */
 #define LLMX_ERR_RANGE 104    /* value outside the weight range the kernels accept */
 #define LLMX_ERR_NOMEM 105    /* device or host allocation failed */
 #define LLMX_ERR_IO 106       /* checkpoint file missing or wrong size */
 #define LLMX_ERR_UNSUPPORTED 107
-#define LLMX_ERR_TIMEOUT 108     /* a kernel's bounded wait expired (device error flag) */
+#define LLMX_ERR_TIMEOUT 108     /* a kernel's bounded wait expired (device error flag), or NCCL
+                                    collectives were still pending after LLMX_NCCL_TIMEOUT_MS (the
+                                    communicator is aborted; the context then answers
+                                    LLMX_ERR_STATE until llmx_destroy) */
 
 /* ---- operators: operator_kind_t host:69-91 / cc8_operator_t
  *      include/control_cache_8x64.hpp:252-277 ---- */

@@ -6,6 +6,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -18,6 +19,7 @@
 #include "fixed.cuh"
 #include "host_model.h"
 #include "kernels.cuh"
+#include "stream_watch.h"
 
 using namespace llmx;
 
@@ -70,6 +72,10 @@ struct llmx_ctx {
     llmx_shape s{};
     int dev = 0, rank = 0, size = 1, nsm = 148;
     ncclComm_t comm = nullptr;
+    // NCCL waits of this rank: deadline (LLMX_NCCL_TIMEOUT_MS) and whether the
+    // communicator was aborted (the context then refuses further work)
+    int nccl_timeout_ms = 60000;
+    bool comm_failed = false;
     cudaStream_t stream = nullptr;
     // geometry of this rank
     int hd = 0, G = 0, KV = 0, hq = 0, h0 = 0, Hq = 0, Il = 0, c0 = 0, tpc_max = 0;
@@ -79,8 +85,8 @@ struct llmx_ctx {
     // 256 CTAs, oversubscribe the SMs and stay on 8-CTA clusters)
     int tpc_max_wide = 0;
     bool attn_wide = false;
-    int attn_rows_min = 2;
-    bool attn_rows_wide = false;  // all-rows kernel on 16-CTA clusters (LLMX_ATTN_ROWS_WIDE)  // blocks of at least this many rows use the all-rows attention kernel (LLMX_ATTN_ROWS_MIN)
+    int attn_rows_min = 2;  // blocks of at least this many rows use the all-rows attention kernel (LLMX_ATTN_ROWS_MIN)
+    bool attn_rows_wide = false;  // all-rows kernel on 16-CTA clusters (LLMX_ATTN_ROWS_WIDE)
     int attn_wide_div = 1;  // wide clusters while rows x heads x 16 CTAs <= SMs / div (LLMX_ATTN_WIDE_DIV)
     // weights: per layer [QKV | O | GU | D] words
     size_t w_qkv = 0, w_o = 0, w_gu = 0, w_d = 0, layer_words = 0;
@@ -134,8 +140,8 @@ struct llmx_ctx {
     bool mma = false;
     int mma_min_rows = 3;
     // projections on the tensor cores: bits MP_QKV, MP_O, MP_GU, MP_D (LLMX_MMA_PROJ).
-    // Default Gate/Up + Down: measured on B200 at 8 rows, Gate/Up 34.6 vs 39.0 us and
-    // Down 21.1 vs 31.0 us on the tensor cores, while QKV (11.2 vs 10.0) and O (12.0
+    // Default Gate/Up + Down: measured on B200 at 8 rows, Gate/Up 26.5 vs 39.0 us and
+    // Down 18.3 vs 31.0 us on the tensor cores, while QKV (11.2 vs 10.0) and O (12.0
     // vs 5.9) are latency bound and stay on the dp2a kernel
     int mma_proj = 0xC;
     MmaGeom mg[4]{};             // QKV, O, Gate/Up, Down of this rank
@@ -180,6 +186,53 @@ int dalloc(llmx_ctx *c, T **p, size_t count) {
     *p = static_cast<T *>(v);
     return LLMX_OK;
 }
+
+// Wait for everything enqueued on the context stream. While the stream can hold
+// NCCL collectives (the set-up exchange, the NCCL all-reduce path) the rank waits
+// with a deadline and watches its communicator: on expiry or an asynchronous
+// error the communicator is aborted, which ends its kernels, and the context
+// refuses further work. The peer all-reduce kernels bound their own waits.
+int stream_wait(llmx_ctx *c) {
+    if (!c->comm || c->ar.n > 1) {
+        CK(cudaStreamSynchronize(c->stream));
+        return LLMX_OK;
+    }
+    cudaError_t qerr = cudaSuccess;
+    ncclResult_t aerr = ncclSuccess;
+    const WatchOutcome w = watch_stream(
+        [&] {
+            qerr = cudaStreamQuery(c->stream);
+            return qerr == cudaSuccess ? 0 : qerr == cudaErrorNotReady ? 1 : -1;
+        },
+        [&] { return ncclCommGetAsyncError(c->comm, &aerr) != ncclSuccess || aerr != ncclSuccess; },
+        [&] {
+            ncclCommAbort(c->comm);
+            c->comm = nullptr;
+            c->comm_failed = true;
+        },
+        [] {
+            return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch())
+                .count();
+        },
+        (double)c->nccl_timeout_ms);
+    switch (w) {
+    case kWatchDone: return LLMX_OK;
+    case kWatchStreamError: return fail_cuda(qerr, "cudaStreamQuery");
+    case kWatchCommError:
+        g_last_error = std::string("NCCL asynchronous error: ") + ncclGetErrorString(aerr) + "; communicator aborted";
+        return LLMX_ERR_NCCL;
+    default:
+        g_last_error = "collective still pending after " + std::to_string(c->nccl_timeout_ms) +
+                       " ms (LLMX_NCCL_TIMEOUT_MS); communicator aborted";
+        return LLMX_ERR_TIMEOUT;
+    }
+}
+
+#define SYNC(c)                          \
+    do {                                 \
+        int rc_ = stream_wait(c);        \
+        if (rc_ != LLMX_OK) return rc_;  \
+    } while (0)
 
 int16_t *kc_layer(const llmx_ctx *c, uint32_t layer) {
     return c->kc + (size_t)layer * c->s.kv_heads * c->s.max_seq * c->hd;
@@ -618,6 +671,10 @@ int check_device_error(llmx_ctx *c) {
 }
 
 bool model_ready(const llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count) {
+    if (c->comm_failed) {
+        g_last_error = "the tensor-parallel communicator was aborted; destroy the context";
+        return false;
+    }
     if (!c->norms_loaded) return false;
     for (uint32_t l = layer_begin; l < layer_begin + layer_count; l++)
         if (!c->layer_loaded[l]) return false;
@@ -702,7 +759,7 @@ int setup_peer_allreduce(llmx_ctx *c, bool want_peer) {
     }
     CK(cudaMemcpy(hbuf + (size_t)c->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice));
     CKN(ncclAllGather(hbuf + (size_t)c->rank * sizeof(mine), hbuf, sizeof(mine), ncclChar, c->comm, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     std::vector<cudaIpcMemHandle_t> all(c->size);
     CK(cudaMemcpy(all.data(), hbuf, all.size() * sizeof(mine), cudaMemcpyDeviceToHost));
     ArPeers a{};
@@ -722,7 +779,7 @@ int setup_peer_allreduce(llmx_ctx *c, bool want_peer) {
     }
     CK(cudaMemcpy(okbuf, &ok, sizeof(int), cudaMemcpyHostToDevice));
     CKN(ncclAllReduce(okbuf, okbuf, 1, ncclInt32, ncclMin, c->comm, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     CK(cudaMemcpy(&ok, okbuf, sizeof(int), cudaMemcpyDeviceToHost));
     if (!ok) {
         for (char *q : c->ar_opened) cudaIpcCloseMemHandle(q);
@@ -974,6 +1031,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         c->qk_scale = qk_scale_q1616(hd);
     }
     if (tp_size > 1) {
+        c->nccl_timeout_ms = env_int("LLMX_NCCL_TIMEOUT_MS", 60000, 1, 3600 * 1000);
         ncclUniqueId id;
         std::memcpy(&id, tp_id, sizeof(id));
         ncclResult_t r = ncclCommInitRank(&c->comm, tp_size, id, tp_rank);
@@ -1033,7 +1091,7 @@ int llmx_upload_layer(llmx_ctx *c, uint32_t layer, const int16_t *dense) {
         CK(launch_mma_wsum(c->staging + off[6], s.inter, c->c0, c->Il, g[MP_D].C, c->mma_rows[MP_D], g[MP_D].T,
                            ws + g[MP_D].wsum_offset, c->stream));
     }
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     c->layer_loaded[layer] = true;
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.first);
     c->graphs.clear();
@@ -1065,7 +1123,7 @@ int llmx_reset_kv(llmx_ctx *c) {
     const size_t n = (size_t)c->s.layers * c->s.kv_heads * c->s.max_seq * c->hd * 2;
     CK(cudaMemsetAsync(c->kc, 0, n, c->stream));
     CK(cudaMemsetAsync(c->vc, 0, n, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return LLMX_OK;
 }
 
@@ -1087,7 +1145,7 @@ static int kv_copy(llmx_ctx *c, uint32_t layer, uint32_t position, uint32_t coun
             CK(cudaMemcpyAsync(hv, dv, n, cudaMemcpyDeviceToHost, c->stream));
         }
     }
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return LLMX_OK;
 }
 
@@ -1105,7 +1163,7 @@ int llmx_write_hidden(llmx_ctx *c, uint32_t pair, const int16_t *rows_host, uint
     CK(cudaSetDevice(c->dev));
     CK(cudaMemcpyAsync(c->hid[pair], rows_host, (size_t)rows * c->s.hidden * 2, cudaMemcpyHostToDevice,
                        c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return LLMX_OK;
 }
 
@@ -1114,7 +1172,7 @@ int llmx_read_hidden(llmx_ctx *c, uint32_t pair, int16_t *rows_host, uint32_t ro
     CK(cudaSetDevice(c->dev));
     CK(cudaMemcpyAsync(rows_host, c->hid[pair], (size_t)rows * c->s.hidden * 2, cudaMemcpyDeviceToHost,
                        c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return LLMX_OK;
 }
 
@@ -1141,7 +1199,7 @@ int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint3
     if (!rc) rc = enqueue_task(c, op, layer, rows, c->in_pair, c->out_pair, ar_next, false, pend);
     if (rc) return rc;
     c->ar_count += task_allreduces(c, op);
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     c->last_launches = c->launches - before;
     return check_device_error(c);
 }
@@ -1234,7 +1292,7 @@ int llmx_run_feature(llmx_ctx *c, uint32_t op, const int16_t *lhs, uint32_t rows
         c->launches += 1;
     }
     CK(cudaMemcpyAsync(out, c->feat_out, (size_t)rows * out_dim * 2, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     c->last_launches = c->launches - before;
     return check_device_error(c);
 }
@@ -1277,7 +1335,7 @@ int llmx_run_prefill_attention_block(llmx_ctx *c, const int16_t *query, uint32_t
     CK(launch_attention(c, t, rows));
     c->launches += 1;
     CK(cudaMemcpyAsync(rowbuf.data(), c->att, rowbuf.size() * 2, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     c->last_launches = c->launches - before;
     if ((rc = check_device_error(c))) return rc;
     for (int p = 0; p < KVh; p++)
@@ -1316,7 +1374,7 @@ int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t la
     if (materialize)
         CK(cudaMemcpyAsync(hidden_out, c->hid[include_final_norm ? 0 : 1], (size_t)rows * c->s.hidden * 2,
                            cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     if ((rc = check_device_error(c))) return rc;
     if (last) {
         const uint32_t op = include_final_norm ? LLMX_OP_FINAL_NORM : LLMX_OP_FFN_SUBLAYER;
@@ -1329,7 +1387,7 @@ int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t la
 int llmx_synchronize(llmx_ctx *c) {
     if (!c) return LLMX_ERR_ARG;
     CK(cudaSetDevice(c->dev));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return check_device_error(c);
 }
 
@@ -1430,7 +1488,7 @@ int llmx_selftest_ar_timeout(llmx_ctx *c, uint32_t poll_limit) {
     if ((rc = set_step(c, 0, 1))) return rc;
     ArFinishArgs f{a, 0, c->hid[1], c->hid[0], c->step, c->err};
     CK(launch_ar_finish(f, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return check_device_error(c);
 }
 
@@ -1549,7 +1607,7 @@ int llmx_generate(llmx_ctx *c, const uint32_t *prompt, uint32_t n_prompt, uint32
     if (last_block_out)
         CK(cudaMemcpyAsync(last_block_out, c->gen_rows, (size_t)last_rows * H * 2, cudaMemcpyDeviceToHost,
                            c->stream));
-    CK(cudaStreamSynchronize(c->stream));
+    SYNC(c);
     return check_device_error(c);
 }
 
