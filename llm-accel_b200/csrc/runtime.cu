@@ -1239,7 +1239,8 @@ int llmx_run_feature(llmx_ctx *c, uint32_t op, const int16_t *lhs, uint32_t rows
     const size_t width = (size_t)std::max(s.hidden, s.inter);
     const size_t slots = std::max<size_t>({(size_t)c->Hq + 2 * c->KV, (size_t)2 * c->Il, (size_t)s.hidden});
     int rc = LLMX_OK;
-    if (!c->feat_lhs && ((rc = dalloc(c, &c->feat_lhs, kMaxRows * width)) ||
+    // feat_sums is allocated last: a failed allocation is retried as a whole on the next call
+    if (!c->feat_sums && ((rc = dalloc(c, &c->feat_lhs, kMaxRows * width)) ||
                          (rc = dalloc(c, &c->feat_rhs, kMaxRows * width)) ||
                          (rc = dalloc(c, &c->feat_out, kMaxRows * width)) ||
                          (rc = dalloc(c, &c->feat_sums, kMaxRows * slots))))
