@@ -570,38 +570,48 @@ cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cud
     }
 }
 
+// Dynamic shared memory limit and, when carveout >= 0, the preferred shared
+// memory carveout (percent of the SM's unified L1 / shared storage) of one
+// instantiation.
+template <int R, int EPI, int VPL, int P>
+static cudaError_t configure_v(int bytes, int carveout) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, VPL, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && carveout >= 0)
+        e = cudaFuncSetAttribute(k_gemv<R, EPI, VPL, P>, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+    return e;
+}
+
 template <int R, int EPI>
-static cudaError_t configure_r(int bytes) {
-    constexpr auto kAttr = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<R, EPI, 8, 1>, kAttr, bytes);
+static cudaError_t configure_r(int bytes, int carveout) {
+    cudaError_t e = configure_v<R, EPI, 8, 1>(bytes, carveout);
     if (e) return e;
     if constexpr (EPI == EPI_RESID || EPI == EPI_PARTIAL) {
         if (R <= 2) {
-            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 1>, kAttr, bytes))) return e;
-            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 4>, kAttr, bytes))) return e;
-            if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 43, 2>, kAttr, bytes))) return e;
+            if ((e = configure_v<R, EPI, 43, 1>(bytes, carveout))) return e;
+            if ((e = configure_v<R, EPI, 43, 4>(bytes, carveout))) return e;
+            if ((e = configure_v<R, EPI, 43, 2>(bytes, carveout))) return e;
         }
-        if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 0, 4>, kAttr, bytes))) return e;
-        if ((e = cudaFuncSetAttribute(k_gemv<R, EPI, 0, 2>, kAttr, bytes))) return e;
+        if ((e = configure_v<R, EPI, 0, 4>(bytes, carveout))) return e;
+        if ((e = configure_v<R, EPI, 0, 2>(bytes, carveout))) return e;
     }
-    return cudaFuncSetAttribute(k_gemv<R, EPI, 0, 1>, kAttr, bytes);
+    return configure_v<R, EPI, 0, 1>(bytes, carveout);
 }
 
 template <int EPI>
-static cudaError_t configure_epi(int bytes) {
+static cudaError_t configure_epi(int bytes, int carveout) {
     cudaError_t e;
-    if ((e = configure_r<1, EPI>(bytes))) return e;
-    if ((e = configure_r<2, EPI>(bytes))) return e;
-    if ((e = configure_r<4, EPI>(bytes))) return e;
-    return configure_r<8, EPI>(bytes);
+    if ((e = configure_r<1, EPI>(bytes, carveout))) return e;
+    if ((e = configure_r<2, EPI>(bytes, carveout))) return e;
+    if ((e = configure_r<4, EPI>(bytes, carveout))) return e;
+    return configure_r<8, EPI>(bytes, carveout);
 }
 
-cudaError_t proj_configure(int max_smem_bytes) {
+cudaError_t proj_configure(int max_smem_bytes, int carveout) {
     cudaError_t e;
-    if ((e = configure_epi<EPI_QKV>(max_smem_bytes))) return e;
-    if ((e = configure_epi<EPI_RESID>(max_smem_bytes))) return e;
-    if ((e = configure_epi<EPI_SILU>(max_smem_bytes))) return e;
-    return configure_epi<EPI_PARTIAL>(max_smem_bytes);
+    if ((e = configure_epi<EPI_QKV>(max_smem_bytes, carveout))) return e;
+    if ((e = configure_epi<EPI_RESID>(max_smem_bytes, carveout))) return e;
+    if ((e = configure_epi<EPI_SILU>(max_smem_bytes, carveout))) return e;
+    return configure_epi<EPI_PARTIAL>(max_smem_bytes, carveout);
 }
 
 }  // namespace llmx

@@ -268,7 +268,9 @@ size_t attn_rows_smem_bytes(int tpc, int cluster);
 size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
-cudaError_t proj_configure(int max_smem_bytes);
+// carveout: preferred shared-memory carveout in percent for every projection
+// kernel, or -1 to leave the driver's choice
+cudaError_t proj_configure(int max_smem_bytes, int carveout);
 size_t gemv_smem_bytes(int rows_tmpl, int epi, int K, int stages, int units_per_chunk, int parts);
 int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int *units_per_chunk, int *parts,
                 int max_warps);
