@@ -109,6 +109,9 @@ struct llmx_ctx {
     uint32_t *o_heads = nullptr;
     Step *step = nullptr;
     int *err = nullptr;
+    // pinned host copy of *err, read on the stream together with a call's results
+    // (null when pinned memory was not available: then read with a blocking copy)
+    int *err_host = nullptr;
     int ring_kb = 96, ring_wide_kb = 176, ring_gu_kb = 160, gemv_ctas_per_sm = 1;
     int gemv_warps = 16;  // consumer warps of a projection CTA at most (LLMX_GEMV_WARPS)
     // preferred shared-memory carveout of the projection kernels in percent
@@ -656,10 +659,9 @@ int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
     return LLMX_OK;
 }
 
-// Kernels record an expired bounded wait in c->err; report and clear it.
-int check_device_error(llmx_ctx *c) {
-    int v = 0;
-    CK(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+// Kernels record an expired bounded wait in c->err; report (v = the value read)
+// and clear it.
+int report_device_error(llmx_ctx *c, int v) {
     if (v != 0) {
         CK(cudaMemset(c->err, 0, sizeof(int)));
         // a call that stopped part-way may leave fused-O sums behind
@@ -672,6 +674,18 @@ int check_device_error(llmx_ctx *c) {
         return LLMX_ERR_TIMEOUT;
     }
     return LLMX_OK;
+}
+
+// End of a synchronous call: the device error word is copied on the stream
+// behind the call's work, so one stream wait covers both (no second round trip
+// to the device after the wait), then reported.
+int finish(llmx_ctx *c) {
+    if (c->err_host) CK(cudaMemcpyAsync(c->err_host, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    SYNC(c);
+    int v = 0;
+    if (c->err_host) v = *c->err_host;
+    else CK(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    return report_device_error(c, v);
 }
 
 bool model_ready(const llmx_ctx *c, uint32_t layer_begin, uint32_t layer_count) {
@@ -808,6 +822,7 @@ void release(llmx_ctx *c) {
     c->ar_opened.clear();
     if (c->comm) ncclCommDestroy(c->comm);
     for (void *p : c->allocations) cudaFree(p);
+    if (c->err_host) cudaFreeHost(c->err_host);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -930,6 +945,10 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         (rc = dalloc(c, &c->o_acc, kMaxRows * H)) ||
         (rc = dalloc(c, &c->step, 1)) || (rc = dalloc(c, &c->err, 1)))
         return bail(rc);
+    if (cudaHostAlloc(&c->err_host, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+        c->err_host = nullptr;  // finish() falls back to a blocking read
+        (void)cudaGetLastError();
+    }
     // head-major O weights for the fused decode attention (w_o words per layer);
     // without the memory the O projection stays a kernel of its own
     if (c->fuse_o && dalloc(c, &c->o_heads, c->w_o * s.layers) != LLMX_OK) {
@@ -1204,9 +1223,8 @@ int llmx_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t position, uint3
     if (!rc) rc = enqueue_task(c, op, layer, rows, c->in_pair, c->out_pair, ar_next, false, pend);
     if (rc) return rc;
     c->ar_count += task_allreduces(c, op);
-    SYNC(c);
     c->last_launches = c->launches - before;
-    return check_device_error(c);
+    return finish(c);
 }
 
 // Per-operator (feature) modes, ops 1-10 (run_feature host:1088-1130).
@@ -1298,9 +1316,8 @@ int llmx_run_feature(llmx_ctx *c, uint32_t op, const int16_t *lhs, uint32_t rows
         c->launches += 1;
     }
     CK(cudaMemcpyAsync(out, c->feat_out, (size_t)rows * out_dim * 2, cudaMemcpyDeviceToHost, c->stream));
-    SYNC(c);
     c->last_launches = c->launches - before;
-    return check_device_error(c);
+    return finish(c);
 }
 
 // Prefill block attention, op 17 (run_prefill_attention_block host:1647-1690).
@@ -1341,9 +1358,8 @@ int llmx_run_prefill_attention_block(llmx_ctx *c, const int16_t *query, uint32_t
     CK(launch_attention(c, t, rows));
     c->launches += 1;
     CK(cudaMemcpyAsync(rowbuf.data(), c->att, rowbuf.size() * 2, cudaMemcpyDeviceToHost, c->stream));
-    SYNC(c);
     c->last_launches = c->launches - before;
-    if ((rc = check_device_error(c))) return rc;
+    if ((rc = finish(c))) return rc;
     for (int p = 0; p < KVh; p++)
         for (uint32_t r = 0; r < rows; r++)
             for (int g = 0; g < G; g++)
@@ -1380,8 +1396,7 @@ int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t la
     if (materialize)
         CK(cudaMemcpyAsync(hidden_out, c->hid[include_final_norm ? 0 : 1], (size_t)rows * c->s.hidden * 2,
                            cudaMemcpyDeviceToHost, c->stream));
-    SYNC(c);
-    if ((rc = check_device_error(c))) return rc;
+    if ((rc = finish(c))) return rc;
     if (last) {
         const uint32_t op = include_final_norm ? LLMX_OP_FINAL_NORM : LLMX_OP_FFN_SUBLAYER;
         llmx_validate_task(&c->s, op, include_final_norm ? 0 : layer_begin + layer_count - 1, position, rows,
@@ -1393,8 +1408,7 @@ int llmx_stack(llmx_ctx *c, const int16_t *hidden_in, uint32_t rows, uint32_t la
 int llmx_synchronize(llmx_ctx *c) {
     if (!c) return LLMX_ERR_ARG;
     CK(cudaSetDevice(c->dev));
-    SYNC(c);
-    return check_device_error(c);
+    return finish(c);
 }
 
 int llmx_time_kernel(llmx_ctx *c, int kernel, uint32_t layer, uint32_t position, uint32_t rows, int iters,
@@ -1494,8 +1508,7 @@ int llmx_selftest_ar_timeout(llmx_ctx *c, uint32_t poll_limit) {
     if ((rc = set_step(c, 0, 1))) return rc;
     ArFinishArgs f{a, 0, c->hid[1], c->hid[0], c->step, c->err};
     CK(launch_ar_finish(f, c->stream));
-    SYNC(c);
-    return check_device_error(c);
+    return finish(c);
 }
 
 int llmx_decode_fuses_o(const llmx_ctx *c) { return c && use_fuse_o(c, 1) ? 1 : 0; }
@@ -1613,8 +1626,7 @@ int llmx_generate(llmx_ctx *c, const uint32_t *prompt, uint32_t n_prompt, uint32
     if (last_block_out)
         CK(cudaMemcpyAsync(last_block_out, c->gen_rows, (size_t)last_rows * H * 2, cudaMemcpyDeviceToHost,
                            c->stream));
-    SYNC(c);
-    return check_device_error(c);
+    return finish(c);
 }
 
 }  // extern "C"
