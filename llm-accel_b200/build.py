@@ -1,8 +1,12 @@
 """Build libllmx.so (CUDA kernels for sm_100a + C++ host runtime + C ABI).
 
-Usage: python llm-accel_b200/build.py [--force]
+Usage: python llm-accel_b200/build.py [--force] [--timeline]
 The shared library is written next to this file so that it travels with the
-source tree; nothing is installed into site-packages.
+source tree; nothing is installed into site-packages.  --timeline builds the
+measurement variant libllmx_timeline.so instead (-DLLMX_TIMELINE: every launch
+of the path stamps its first CTA start and last warp exit with %globaltimer,
+read back through llmx_timeline_*; see csrc/timeline.cuh), in its own object
+directory; llmx.py loads it when LLMX_TIMELINE=1.
 """
 from __future__ import annotations
 
@@ -52,25 +56,28 @@ def _headers():
     return hs
 
 
-def _compile(src, force):
+def _compile(src, force, build_dir, defines):
     path = os.path.join(CSRC, src)
-    obj = os.path.join(BUILD, src + ".o")
+    obj = os.path.join(build_dir, src + ".o")
     if not force and not _newer(obj, [path] + _headers()):
         return obj
-    cmd = [NVCC, *ARCH, *COMMON, *_nccl()[0], "-c", path, "-o", obj]
+    cmd = [NVCC, *ARCH, *COMMON, *defines, *_nccl()[0], "-c", path, "-o", obj]
     subprocess.run(cmd, check=True)
     return obj
 
 
-def build(force: bool = False) -> str:
-    os.makedirs(BUILD, exist_ok=True)
+def build(force: bool = False, timeline: bool = False) -> str:
+    build_dir = BUILD + "_timeline" if timeline else BUILD
+    lib = os.path.join(HERE, "libllmx_timeline.so") if timeline else LIB
+    defines = ["-DLLMX_TIMELINE"] if timeline else []
+    os.makedirs(build_dir, exist_ok=True)
     with cf.ThreadPoolExecutor(len(SOURCES)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, force), SOURCES))
-    if force or _newer(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, *_nccl()[1], "-lpthread"]
+        objs = list(ex.map(lambda s: _compile(s, force, build_dir, defines), SOURCES))
+    if force or _newer(lib, objs):
+        cmd = [NVCC, *ARCH, "-shared", "-o", lib, *objs, *_nccl()[1], "-lpthread"]
         subprocess.run(cmd, check=True)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv))
+    print(build(force="--force" in sys.argv, timeline="--timeline" in sys.argv))

@@ -110,6 +110,7 @@ size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows) {
 
 template <int C>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(16) char raw[];
     cg::cluster_group cluster = cg::this_cluster();
     const int c = (int)cluster.block_rank();
@@ -402,6 +403,7 @@ constexpr int kAttnRowsThreads = 256;
 
 template <int C>
 __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(16) char raw[];
     cg::cluster_group cluster = cg::this_cluster();
     const int c = (int)cluster.block_rank();
@@ -596,6 +598,7 @@ cudaError_t attn_rows_configure(int max_smem_bytes, int cluster) {
 
 cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
     AttnArgs c = a;
+    LLMX_TL_TAKE(c, "attn_rows");
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cluster * a.q_heads, 1);
@@ -626,6 +629,7 @@ cudaError_t attn_configure(int max_smem_bytes, int cluster) {
 
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     AttnArgs c = a;
+    LLMX_TL_TAKE(c, a.o_w != nullptr ? "attn+o" : "attn");
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cluster * a.q_heads, rows);
@@ -646,3 +650,5 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
 }
 
 }  // namespace llmx
+
+LLMX_TL_READER(attention)

@@ -34,6 +34,7 @@ static __device__ __forceinline__ int feature_slot(int o, int order, int hd) {
 }
 
 __global__ void __launch_bounds__(256) k_feature_round(const FeatureRoundArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     pdl_wait();
     pdl_trigger();
     const int total = a.rows * a.n_out;
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(256) k_feature_round(const FeatureRoundArgs a)
 
 cudaError_t launch_feature_round(const FeatureRoundArgs &a, cudaStream_t s) {
     FeatureRoundArgs c = a;
+    LLMX_TL_TAKE(c, "feature_round");
     void *args[] = {&c};
     int blocks = (a.rows * a.n_out + 255) / 256;
     if (blocks < 1) blocks = 1;
@@ -54,6 +56,7 @@ cudaError_t launch_feature_round(const FeatureRoundArgs &a, cudaStream_t s) {
 // SiLU(lhs) x rhs (stream_silu_mul kernel/compute_stream.cpp:123-164) or the
 // saturating residual add (stream_add :205-225), element by element.
 __global__ void __launch_bounds__(256) k_feature_vec(const FeatureVecArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     pdl_wait();
     pdl_trigger();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x) {
@@ -64,6 +67,7 @@ __global__ void __launch_bounds__(256) k_feature_vec(const FeatureVecArgs a) {
 
 cudaError_t launch_feature_vec(const FeatureVecArgs &a, cudaStream_t s) {
     FeatureVecArgs c = a;
+    LLMX_TL_TAKE(c, "feature_vec");
     void *args[] = {&c};
     int blocks = (a.n + 255) / 256;
     if (blocks < 1) blocks = 1;
@@ -71,3 +75,5 @@ cudaError_t launch_feature_vec(const FeatureVecArgs &a, cudaStream_t s) {
 }
 
 }  // namespace llmx
+
+LLMX_TL_READER(feature)

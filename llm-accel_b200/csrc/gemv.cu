@@ -283,6 +283,7 @@ static __device__ __forceinline__ void unit_range(int nunits, int &u0, int &u1) 
 
 template <int R, int EPI, int VPL, int P>
 __global__ void __launch_bounds__(Warps<R>::kThreads, 1) k_gemv(const ProjArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     constexpr int U = GemvTraits<R, EPI>::U;
     constexpr int N = U * R;  // int64 sums per unit
     extern __shared__ __align__(128) char smem[];
@@ -512,6 +513,7 @@ int gemv_stages(int rows_tmpl, int epi, int K, int max_smem, int ring_bytes, int
 template <int R, int EPI, int VPL, int P>
 static cudaError_t launch_gemv_v(const ProjArgs &a, int grid, cudaStream_t st) {
     ProjArgs c = a;
+    LLMX_TL_TAKE(c, EPI == EPI_QKV ? "gemv/qkv" : EPI == EPI_RESID ? "gemv/resid" : EPI == EPI_SILU ? "gemv/gate_up" : "gemv/partial");
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -615,3 +617,5 @@ cudaError_t proj_configure(int max_smem_bytes, int carveout) {
 }
 
 }  // namespace llmx
+
+LLMX_TL_READER(gemv)

@@ -28,6 +28,7 @@ cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, cudaS
 // Task 20: final RMSNorm of 1..8 rows (stream_rmsnorm compute_stream.cpp:227-288)
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_rmsnorm(const NormArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     __shared__ int64_t red[8];
     __shared__ int32_t inv_s;
     const int rows = load_step(a.step).rows;
@@ -58,6 +59,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const NormArgs a) {
 
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s) {
     NormArgs c = a;
+    LLMX_TL_TAKE(c, "rmsnorm");
     void *args[] = {&c};
     return launch_pdl((const void *)k_rmsnorm, dim3(rows), dim3(256), args, s);
 }
@@ -66,6 +68,7 @@ cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s) {
 // tensor parallel: round the all-reduced exact sums and add the residual
 // --------------------------------------------------------------------------
 __global__ void k_round_resid(const ResidArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     const int rows = load_step(a.step).rows;
     pdl_wait();
     pdl_trigger();
@@ -82,6 +85,7 @@ __global__ void k_round_resid(const ResidArgs a) {
 // every rank, adds the ranks' exact sums (order-free), rounds as round_mac and
 // adds the residual -- the same result on every rank.
 __global__ void __launch_bounds__(256) k_ar_finish(const ArFinishArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     const Step st = load_step(a.step);
     pdl_wait();
     pdl_trigger();
@@ -104,12 +108,14 @@ __global__ void __launch_bounds__(256) k_ar_finish(const ArFinishArgs a) {
 
 cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s) {
     ArFinishArgs c = a;
+    LLMX_TL_TAKE(c, "ar_finish");
     void *args[] = {&c};
     return launch_pdl((const void *)k_ar_finish, dim3((kMaxRows * a.ar.hidden / 4 + 255) / 256), dim3(256), args, s);
 }
 
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s) {
     ResidArgs c = a;
+    LLMX_TL_TAKE(c, "round_resid");
     void *args[] = {&c};
     const int blocks = (rows * a.n + 255) / 256;
     return launch_pdl((const void *)k_round_resid, dim3(blocks), dim3(256), args, s);
@@ -168,3 +174,5 @@ cudaError_t launch_pack_pairs(const int16_t *dense, int ld, int col0, int K,
 }
 
 }  // namespace llmx
+
+LLMX_TL_READER(kernels)

@@ -5,6 +5,8 @@
 #include <string>
 #include <cstdint>
 
+#include "timeline.cuh"
+
 namespace llmx {
 
 constexpr int kTile = 64;     // online-softmax tile: include/control_cache_8x64.hpp:72
@@ -112,6 +114,7 @@ struct ProjArgs {
     // (the fused attention's O sums, read by that kernel's prologue)
     int64_t *zero;
     int zero_n;
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 
 // Tensor-core projection of blocks of 3..8 rows (mma_proj.cu): weights in
@@ -146,6 +149,7 @@ struct MmaArgs {
     int max_items;       // items of the largest CTA range (activation slots)
     int *error;
     const int32_t *wsum; // [T][C+1][128] prefix over chunks of each tile row's weight sums (k_mma_wsum)
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 cudaError_t launch_mma_proj(const MmaArgs &a, int epi, int grid, cudaStream_t s);
 cudaError_t mma_configure(int max_smem_bytes);
@@ -198,6 +202,7 @@ struct AttnArgs {
     int64_t *o_acc;
     int trigger_tiles;   // k_attn: let the next kernel launch at the start when the row's context exceeds
                          // this many 64-position tiles, else once PV is done
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 
 struct NormArgs {
@@ -208,6 +213,7 @@ struct NormArgs {
     int32_t inv_elems;
     int32_t inv_rms_const;
     const Step *step;
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 
 struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduce)
@@ -217,6 +223,7 @@ struct ResidArgs {  // round exact int64 sums + residual (after the TP all-reduc
     int n;
     const Step *step;
     int64_t *clear;      // non-null (== partial): each sum is cleared once read (the fused O sums)
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 
 // Per-operator (feature) kernels, feature.cu.  Slot orders of the packed
@@ -235,6 +242,7 @@ struct FeatureRoundArgs {  // out[r][o] = round_mac(sums[r][slot(o)])
     int n_out;
     int order;
     int hd;
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 struct FeatureVecArgs {  // out = silu ? SiLU(lhs) x rhs : sat16(lhs + rhs), n elements
     const int16_t *lhs;
@@ -243,6 +251,7 @@ struct FeatureVecArgs {  // out = silu ? SiLU(lhs) x rhs : sat16(lhs + rhs), n e
     const int16_t *etab;
     int n;
     int silu;
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 cudaError_t launch_feature_round(const FeatureRoundArgs &a, cudaStream_t s);
 cudaError_t launch_feature_vec(const FeatureVecArgs &a, cudaStream_t s);
@@ -254,6 +263,7 @@ struct ArFinishArgs {  // wait for every rank's sums, add them, round, + residua
     int16_t *out;
     const Step *step;
     int *error;
+    LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 

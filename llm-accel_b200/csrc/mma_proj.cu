@@ -310,6 +310,7 @@ static __device__ void mma_epilogue(const MmaArgs &a, const Step &st, int t, int
 
 template <int EPI>
 __global__ void __launch_bounds__(kMmaThreads, 1) k_mma_proj(const MmaArgs a) {
+    LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(1024) char smem[];
     // header: barriers, flags and the staging reduction (kMmaHdr bytes)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kMmaMaxStages]
@@ -531,6 +532,7 @@ int mma_stages(int max_items, int max_smem) {
 template <int EPI>
 static cudaError_t launch_mma_t(const MmaArgs &a, int grid, cudaStream_t st) {
     MmaArgs c = a;
+    LLMX_TL_TAKE(c, EPI == EPI_QKV ? "mma/qkv" : EPI == EPI_RESID ? "mma/resid" : EPI == EPI_SILU ? "mma/gate_up" : "mma/partial");
     void *args[] = {&c};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -626,3 +628,5 @@ cudaError_t launch_mma_wsum(const int16_t *dense, int ld, int col0, int K, int C
 }
 
 }  // namespace llmx
+
+LLMX_TL_READER(mma_proj)

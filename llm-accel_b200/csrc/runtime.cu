@@ -47,7 +47,8 @@ int fail_cuda(cudaError_t e, const char *what) {
         }                                                                     \
     } while (0)
 
-__global__ void k_set_step(Step *dst, int32_t position, int32_t rows, uint32_t ar_base) {
+__global__ void k_set_step(Step *dst, int32_t position, int32_t rows, uint32_t ar_base LLMX_TL_PARAM) {
+    LLMX_TL_GUARD(tl_slot);
     asm volatile("griddepcontrol.launch_dependents;");
     dst->position = position;
     dst->rows = rows;
@@ -653,7 +654,7 @@ uint32_t task_allreduces(const llmx_ctx *c, uint32_t op) {
 uint32_t stack_allreduces(const llmx_ctx *c, uint32_t layer_count) { return c->size > 1 ? 2u * layer_count : 0u; }
 
 int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
-    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows, c->ar_count);
+    k_set_step<<<1, 1, 0, c->stream>>>(c->step, (int32_t)position, (int32_t)rows, c->ar_count LLMX_TL_ARG("set_step"));
     CK(cudaGetLastError());
     c->launches += 1;
     return LLMX_OK;
@@ -1630,3 +1631,81 @@ int llmx_generate(llmx_ctx *c, const uint32_t *prompt, uint32_t n_prompt, uint32
 }
 
 }  // extern "C"
+
+#ifdef LLMX_TIMELINE
+// ---------------------------------------------------------------------------
+// Launch timeline (measurement builds only; see timeline.cuh).  Slots are taken
+// for the life of the process, so a graph captured earlier keeps reporting
+// under the names its launches took at capture.
+// ---------------------------------------------------------------------------
+namespace llmx {
+static std::mutex g_tl_mu;
+static std::vector<std::string> g_tl_names;
+
+int tl_take(const char *name) {
+    std::lock_guard<std::mutex> lock(g_tl_mu);
+    if ((int)g_tl_names.size() >= kTlSlots) return -1;
+    g_tl_names.emplace_back(name);
+    return (int)g_tl_names.size() - 1;
+}
+}  // namespace llmx
+
+LLMX_TL_READER(runtime)
+extern "C" int llmx_tl_table_kernels(void *, int, int);
+extern "C" int llmx_tl_table_gemv(void *, int, int);
+extern "C" int llmx_tl_table_attention(void *, int, int);
+extern "C" int llmx_tl_table_mma_proj(void *, int, int);
+extern "C" int llmx_tl_table_feature(void *, int, int);
+
+namespace {
+using TlReader = int (*)(void *, int, int);
+const TlReader kTlReaders[] = {llmx_tl_table_runtime, llmx_tl_table_kernels, llmx_tl_table_gemv,
+                               llmx_tl_table_attention, llmx_tl_table_mma_proj, llmx_tl_table_feature};
+}  // namespace
+
+extern "C" {
+
+// Clear every stamp on the context's device (after the work enqueued so far).
+int llmx_timeline_reset(llmx_ctx *c) {
+    if (!c) return LLMX_ERR_ARG;
+    CK(cudaSetDevice(c->dev));
+    SYNC(c);
+    for (TlReader rd : kTlReaders) CK((cudaError_t)rd(nullptr, 0, 1));
+    return LLMX_OK;
+}
+
+// Number of slots taken so far in this process.
+int llmx_timeline_slots(void) {
+    std::lock_guard<std::mutex> lock(g_tl_mu);
+    return (int)g_tl_names.size();
+}
+
+// Name under which slot `slot` was taken ("" for an unknown slot).
+const char *llmx_timeline_name(int slot) {
+    std::lock_guard<std::mutex> lock(g_tl_mu);
+    return slot >= 0 && slot < (int)g_tl_names.size() ? g_tl_names[slot].c_str() : "";
+}
+
+// Stamps of slots [0, n) on the context's device after the stream's work:
+// out[2*s] = first CTA start, out[2*s+1] = last warp exit (%globaltimer ns);
+// a slot that did not run since the last reset reads start = ~0, end = 0.
+int llmx_timeline_read(llmx_ctx *c, unsigned long long *out, int n) {
+    if (!c || !out || n < 0) return LLMX_ERR_ARG;
+    if (n > kTlSlots) n = kTlSlots;
+    CK(cudaSetDevice(c->dev));
+    SYNC(c);
+    std::vector<TlEntry> merged((size_t)n, TlEntry{~0ull, 0ull}), part((size_t)n);
+    for (TlReader rd : kTlReaders) {
+        CK((cudaError_t)rd(part.data(), n, 0));
+        for (int s = 0; s < n; s++)
+            if (part[s].start != ~0ull) merged[s] = part[s];
+    }
+    for (int s = 0; s < n; s++) {
+        out[2 * s] = merged[s].start;
+        out[2 * s + 1] = merged[s].end;
+    }
+    return LLMX_OK;
+}
+
+}  // extern "C"
+#endif  // LLMX_TIMELINE

@@ -19,7 +19,10 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libllmx.so")
+# LLMX_TIMELINE=1 loads the measurement build (build.py --timeline): the same
+# kernels, each launch stamping its start and end for llmx_timeline_read.
+TIMELINE = os.environ.get("LLMX_TIMELINE") == "1"
+LIB_PATH = os.path.join(HERE, "libllmx_timeline.so" if TIMELINE else "libllmx.so")
 
 OK = 0
 BAD_OPERATOR, BAD_TOKEN_COUNT, BAD_TILE_LENGTH, BAD_POSITION, BAD_LAYER = 1, 2, 3, 4, 5
@@ -141,6 +144,14 @@ def lib():
             "llmx_selftest_ar_timeout": (C.c_int, [vp, C.c_uint32]),
             "llmx_generate": (C.c_int, [vp, u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp]),
         }
+        if TIMELINE:
+            sig.update({
+                "llmx_timeline_reset": (C.c_int, [vp]),
+                "llmx_timeline_slots": (C.c_int, []),
+                "llmx_timeline_name": (C.c_char_p, [C.c_int]),
+                "llmx_timeline_read": (C.c_int, [vp, np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS"),
+                                                 C.c_int]),
+            })
         for name, (res, args) in sig.items():
             f = getattr(L, name)
             f.restype = res
@@ -307,6 +318,20 @@ class Accelerator:
 
     def upload_model(self, m: Model):
         check(lib().llmx_upload_model(self.h, m.h), "upload_model")
+
+    # measurement build only (LLMX_TIMELINE=1)
+    def timeline_reset(self):
+        check(lib().llmx_timeline_reset(self.h), "timeline_reset")
+
+    def timeline_read(self):
+        """Launches that ran since timeline_reset(), in start order: (slot,
+        name, start_ns, end_ns) from %globaltimer on this context's device."""
+        n = lib().llmx_timeline_slots()
+        out = np.zeros(2 * max(n, 1), np.uint64)
+        check(lib().llmx_timeline_read(self.h, out, n), "timeline_read")
+        runs = [(s, lib().llmx_timeline_name(s).decode(), int(out[2 * s]), int(out[2 * s + 1]))
+                for s in range(n) if int(out[2 * s]) != 0xFFFFFFFFFFFFFFFF]
+        return sorted(runs, key=lambda r: r[2])
 
     def upload_layer(self, layer, dense):
         check(lib().llmx_upload_layer(self.h, layer, np.ascontiguousarray(dense, np.int16).reshape(-1)),

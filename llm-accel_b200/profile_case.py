@@ -11,7 +11,15 @@ weights), preloads a seeded KV cache to `--position`, then
   --generate: greedy generation on the device (llmx_generate: k_embed_rows,
             the stack, k_lm_scan + k_lm_pick) over `--layers` layers, 8 prompt
             tokens and `--steps` new tokens.
+  --timeline: after `--steps` warm-up stack calls (graph capture), one more
+            `--rows`-row stack call whose launches stamp %globaltimer (the
+            measurement build: `python llm-accel_b200/build.py --timeline` and
+            LLMX_TIMELINE=1); prints every launch's start, duration and the idle
+            gap before it, in graph order, plus per-kernel totals.  Under
+            torchrun (WORLD_SIZE > 1) every rank runs its tensor-parallel shard
+            (CUDA device = LOCAL_RANK) and prints its own line.
 Usage: python llm-accel_b200/profile_case.py --layers 4 --position 512 --table
+       LLMX_TIMELINE=1 python llm-accel_b200/profile_case.py --layers 36 --position 512 --max-seq 640 --timeline
 """
 from __future__ import annotations
 
@@ -41,6 +49,7 @@ def main():
     ap.add_argument("--iters", type=int, default=40)
     ap.add_argument("--argmax", action="store_true")
     ap.add_argument("--generate", action="store_true")
+    ap.add_argument("--timeline", action="store_true")
     ap.add_argument("--kv-scale", type=float, default=600.0, help="std of the preloaded KV cache (raw Q8.8)")
     ap.add_argument("--hidden", type=int, default=0, help="override the shape (e.g. a tensor-parallel rank's heads)")
     ap.add_argument("--heads", type=int, default=0)
@@ -55,7 +64,15 @@ def main():
                               ("inter", args.inter)) if v}
     s = llmx.shape("qwen2.5-3b", layers=args.layers, max_seq=args.max_seq, **over)
     m = llmx.Model(s).init_gaussian(20260718, 0.02)
-    acc = llmx.Accelerator(s)
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    tp = {}
+    if world > 1:  # tensor parallel: the NCCL id travels over a gloo group (torchrun's env rendezvous)
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method="env://")
+        obj = [llmx.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        tp = dict(device=int(os.environ.get("LOCAL_RANK", "0")), tp_rank=rank, tp_size=world, tp_id=obj[0])
+    acc = llmx.Accelerator(s, **tp)
     acc.upload_model(m)
     rng = np.random.default_rng(0)
     P = args.position
@@ -86,7 +103,35 @@ def main():
             acc.bind(0, 1)
             acc.task(llmx.OP_FINAL_NORM, 0, pos, args.rows)
         print("eager steps done")
+    if args.timeline:
+        timeline_case(acc, m, s, P, args, rank, world, rng)
     acc.close()
+
+
+def timeline_case(acc, m, s, P, args, rank, world, rng):
+    if not llmx.TIMELINE:
+        raise SystemExit("--timeline needs the measurement build: build.py --timeline, then LLMX_TIMELINE=1")
+    R = args.rows
+    hs = m.embed(rng.integers(0, s.vocab, R * (args.steps + 1)))
+    for step in range(args.steps):  # graph capture and warm-up
+        acc.stack(hs[step * R:(step + 1) * R], position=P + step * R)
+    pos = P + args.steps * R
+    acc.timeline_reset()
+    acc.stack(hs[args.steps * R:], position=pos)
+    runs = acc.timeline_read()
+    t0 = runs[0][2]
+    launches, per_name, busy_end = [], {}, t0
+    for slot, name, st, en in runs:
+        launches.append({"name": name, "start_us": round((st - t0) / 1e3, 2), "dur_us": round((en - st) / 1e3, 2),
+                         "idle_before_us": round(max(0, st - busy_end) / 1e3, 2)})
+        busy_end = max(busy_end, en)
+        d = per_name.setdefault(name, {"launches": 0, "sum_dur_us": 0.0})
+        d["launches"] += 1
+        d["sum_dur_us"] = round(d["sum_dur_us"] + (en - st) / 1e3, 2)
+    print(json.dumps({"rank": rank, "world": world, "layers": s.layers, "rows": R, "position": pos,
+                      "step_us": round((busy_end - t0) / 1e3, 2),
+                      "idle_us": round(sum(x["idle_before_us"] for x in launches), 2),
+                      "per_kernel": per_name, "launches": launches}))
 
 
 def generate_case(layers, steps):
