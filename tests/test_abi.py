@@ -24,6 +24,29 @@ def test_library_exports_header_symbols(llmx):
     assert not missing, f"declared but not exported: {missing}"
 
 
+def test_timeline_only_in_the_measurement_build(tmp_path):
+    """The launch timeline (csrc/timeline.cuh) exists only when compiled with
+    -DLLMX_TIMELINE: the product library exports none of its symbols, and the
+    instrumented form of the header and of an argument struct compiles."""
+    lib = C.CDLL(os.path.join(ROOT, "llm-accel_b200", "libllmx.so"))
+    assert not hasattr(lib, "llmx_timeline_read") and not hasattr(lib, "llmx_tl_table_gemv")
+    nvcc = "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("nvcc not available")
+    src = tmp_path / "tl_probe.cu"
+    src.write_text('#include "kernels.cuh"\n'
+                   "__global__ void k_probe(const llmx::NormArgs a) { LLMX_TL_GUARD(a.tl_slot); }\n"
+                   "int llmx::tl_take(const char *) { return 0; }\n"
+                   "void probe_take(llmx::NormArgs &a) { LLMX_TL_TAKE(a, \"probe\"); }\n"
+                   "LLMX_TL_READER(probe)\n")
+    csrc = os.path.join(ROOT, "llm-accel_b200", "csrc")
+    import subprocess
+    r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-DLLMX_TIMELINE",
+                        "-I", csrc, "-I", os.path.join(ROOT, "include"), "-c", str(src), "-o",
+                        str(tmp_path / "tl_probe.o")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
 def test_profiles(llmx, oracle):
     for name, vals in oracle.PROFILES.items():
         assert llmx.profile(name).tuple() == vals
