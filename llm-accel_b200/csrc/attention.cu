@@ -81,34 +81,48 @@ struct AttnSmem {      // carved out of dynamic shared memory
 
 static __host__ __device__ size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
-static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, int o_rows, size_t off[12]) {
+// split = false: the O slice reuses the K/V buffer once PV is done (the same
+// bytes: the CTA count per SM stays that of attention alone, which keeps every
+// cluster of the grid resident at once), and each CTA holds the tile values of
+// the hd/cl output elements it finalises.  split = true (the k_attn<C, true>
+// variant): the O slice has a buffer of its own, filled from the kernel's start,
+// and every CTA holds the tile values of all hd elements.
+static __host__ __device__ size_t attn_layout(int tpc, int hd, int cl, int o_rows, size_t off[12],
+                                              bool split = false) {
     const size_t rows = (size_t)tpc * kTile;
     size_t b = 0;
-    // kv, later the O slice (the same bytes: the CTA count per SM stays that of
-    // attention alone, which keeps every cluster of the grid resident at once)
-    off[0] = b; b = align16(b + (rows > (size_t)o_rows ? rows : (size_t)o_rows) * kMaxHd * 2);
+    const size_t kv_rows = split || rows > (size_t)o_rows ? rows : (size_t)o_rows;
+    off[0] = b; b = align16(b + kv_rows * kMaxHd * 2);                       // kv (+ O slice)
     off[1] = b; b = align16(b + kPtabChunks * 16);                           // ptab
     off[2] = b; b = align16(b + (size_t)kMaxHd * 2);                         // q
     off[3] = b; b = align16(b + rows * 2);                                   // sc
-    off[4] = b; b = align16(b + (size_t)kMaxTiles * (kMaxHd / cl) * 2);      // tvr
+    off[4] = b; b = align16(b + (size_t)kMaxTiles * (split ? kMaxHd : kMaxHd / cl) * 2);  // tvr
     off[5] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // mloc
     off[6] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gsum
     off[7] = b; b = align16(b + (size_t)kMaxTiles * 4);                      // gold
     off[8] = b; b = align16(b + (size_t)tpc * 4);                            // tsum
     off[9] = b; b = align16(b + 3 * 8);                                      // bar
     off[10] = b; b = align16(b + (size_t)kMaxHd * 2);                        // att
-    off[11] = off[0];                                                        // ow
+    if (split) {
+        off[11] = b; b = align16(b + (size_t)o_rows * kMaxHd * 2);           // ow
+    } else {
+        off[11] = off[0];                                                    // ow
+    }
     (void)hd;
     return b;
 }
 
-size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows) {
+size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows, bool split) {
     size_t off[12];
-    return attn_layout(tpc, hd, cluster, o_rows, off);
+    return attn_layout(tpc, hd, cluster, o_rows, off, split);
 }
 
 
-template <int C>
+// kSplit (O projection fused only, LLMX_ATTN_SPLIT_O): the O slice is copied
+// into a buffer of its own from the kernel's start, and the PV tile values go
+// to every CTA, which then runs the recurrence of all hd elements itself -- no
+// third cluster barrier (the head-output exchange) before the O rows.
+template <int C, bool kSplit>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(16) char raw[];
@@ -118,7 +132,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     const int r = blockIdx.y;
     const int hd = a.hd, vpr = hd >> 3, epc = hd / C;  // elements finalised per CTA
     size_t off[12];
-    attn_layout(a.tpc_max, hd, C, a.o_w != nullptr ? a.o_rows : 0, off);
+    attn_layout(a.tpc_max, hd, C, a.o_w != nullptr ? a.o_rows : 0, off, kSplit);
     AttnSmem m;
     m.kv = reinterpret_cast<int16_t *>(raw + off[0]);
     m.ptab = reinterpret_cast<int16_t *>(raw + off[1]);
@@ -148,7 +162,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         mbar_init(m.bar + 1, 1);
         mbar_init(m.bar + 2, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        if (fuse_o) l2_prefetch_slice(reinterpret_cast<const char *>(ow_src), ow_bytes, 0, 1);
+        if constexpr (kSplit) {
+            if (fuse_o) {  // waited for before the O rows (every path that issued it reaches that wait)
+                mbar_expect_tx(m.bar + 2, ow_bytes);
+                bulk_g2s(m.ow, ow_src, ow_bytes, m.bar + 2);
+            }
+        } else {
+            if (fuse_o) l2_prefetch_slice(reinterpret_cast<const char *>(ow_src), ow_bytes, 0, 1);
+        }
     }
     __syncthreads();
     // the next kernel (Gate/Up or O) may launch -- and stream its weights on the
@@ -296,40 +317,59 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         int32_t ts = sat32((int64_t)b0 + b1 + b2 + b3);
         ts = sat32(rnd((int64_t)ts * 1024, 16));
         const int16_t tv = (int16_t)sat16(rnd(ts, 8));
-        *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
+        if constexpr (kSplit) {  // every CTA runs the whole recurrence
+            for (int k = 0; k < C; k++) *cluster.map_shared_rank(m.tvr + (t_begin + tli) * hd + e, k) = tv;
+        } else {
+            *cluster.map_shared_rank(m.tvr + (t_begin + tli) * epc + e / C, e % C) = tv;
+        }
     }
     cluster.sync();
     if (!early_trigger) pdl_trigger();
-    if (fuse_o && threadIdx.x == 0) {  // V is consumed: the buffer now receives the O slice
+    if (!kSplit && fuse_o && threadIdx.x == 0) {  // V is consumed: the buffer now receives the O slice
         mbar_expect_tx(m.bar + 2, ow_bytes);
         bulk_g2s(m.ow, ow_src, ow_bytes, m.bar + 2);
     }
 
     // ---- 3. in-order Q16.16 recurrence on local shared memory ---------------
-    for (int j = threadIdx.x; ntiles > 0 && j < epc; j += blockDim.x) {
-        const int e = j * C + c;
-        int32_t sum = 0, acc = 0;
-        for (int u = 0; u < ntiles; u++) {
-            const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
-            sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[u]);
-            acc = sat32(rnd((int64_t)acc * o, 16));
-            acc = sat32((int64_t)acc + (int64_t)m.tvr[u * epc + j] * 256);
+    if constexpr (kSplit) {  // all hd elements in every CTA (the host launches this variant with o_w only)
+        for (int e = threadIdx.x; ntiles > 0 && e < hd; e += blockDim.x) {
+            int32_t sum = 0, acc = 0;
+            for (int u = 0; u < ntiles; u++) {
+                const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
+                sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[u]);
+                acc = sat32(rnd((int64_t)acc * o, 16));
+                acc = sat32((int64_t)acc + (int64_t)m.tvr[u * hd + e] * 256);
+            }
+            const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
+            m.att[e] = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
         }
-        const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
-        const int16_t y = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
-        if (a.o_w == nullptr) {
-            a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = y;
-        } else {  // the head output -> every CTA of the cluster
-            for (int k = 0; k < C; k++) *cluster.map_shared_rank(m.att + e, k) = y;
+        __syncthreads();  // after the second cluster barrier no CTA writes another's shared memory
+    } else {
+        for (int j = threadIdx.x; ntiles > 0 && j < epc; j += blockDim.x) {
+            const int e = j * C + c;
+            int32_t sum = 0, acc = 0;
+            for (int u = 0; u < ntiles; u++) {
+                const int64_t o = (int64_t)m.gold[u] * 4;  // Q2.14 -> Q16.16
+                sum = sat32(rnd((int64_t)sum * o, 16) + m.gsum[u]);
+                acc = sat32(rnd((int64_t)acc * o, 16));
+                acc = sat32((int64_t)acc + (int64_t)m.tvr[u * epc + j] * 256);
+            }
+            const int64_t inv = sat16(rnd((int64_t)recip_q16(sum < 16 ? 16 : sum), 8));
+            const int16_t y = (int16_t)sat16(rnd((int64_t)acc * inv * 256, 24));
+            if (a.o_w == nullptr) {
+                a.out[(size_t)r * a.q_heads * hd + (size_t)lh * hd + e] = y;
+            } else {  // the head output -> every CTA of the cluster
+                for (int k = 0; k < C; k++) *cluster.map_shared_rank(m.att + e, k) = y;
+            }
         }
+        if (a.o_w == nullptr) return;
+        cluster.sync();
     }
-    if (a.o_w == nullptr) return;
 
     // ---- 4. fused O projection: this head's exact partial of this CTA's O rows ----
     // (golden_projection host:3105-3142 sums int16 x int16 products exactly and
     // rounds once; the sum over heads is completed by int64 atomics and rounded,
     // with the residual, by the next kernel's prologue)
-    cluster.sync();
     if (!fuse_o) return;
     if (!mbar_wait(m.bar + 2, 0)) {
         atomicCAS(a.error, 0, kErrAttnCopy);
@@ -620,11 +660,37 @@ cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
 
 cudaError_t attn_configure(int max_smem_bytes, int cluster) {
     if (cluster == kClusterWide) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn<kClusterWide>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_attn<kClusterWide, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        return cudaFuncSetAttribute(k_attn<kClusterWide>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+        return cudaFuncSetAttribute(k_attn<kClusterWide, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    max_smem_bytes);
     }
-    return cudaFuncSetAttribute(k_attn<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+    return cudaFuncSetAttribute(k_attn<kCluster, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+}
+
+cudaError_t attn_split_configure(int smem_bytes, int q_heads, int *ok) {
+    *ok = 0;
+    cudaError_t e =
+        cudaFuncSetAttribute(k_attn<kCluster, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    // every cluster of the one-row grid must be resident at once
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kCluster * q_heads, 1);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, (const void *)k_attn<kCluster, true>, &cfg);
+    if (e != cudaSuccess) return e;
+    *ok = clusters >= q_heads ? 1 : 0;
+    return cudaSuccess;
 }
 
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
@@ -634,7 +700,9 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cluster * a.q_heads, rows);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster, a.o_w != nullptr ? a.o_rows : 0);
+    // the split variant only for the fused O projection on 8-CTA clusters
+    const bool split = a.split_o && a.o_w != nullptr && a.cluster == kCluster;
+    cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster, a.o_w != nullptr ? a.o_rows : 0, split);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -645,7 +713,9 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn<kClusterWide> : (const void *)k_attn<kCluster>;
+    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn<kClusterWide, false>
+                     : split                      ? (const void *)k_attn<kCluster, true>
+                                                  : (const void *)k_attn<kCluster, false>;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

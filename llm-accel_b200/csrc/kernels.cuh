@@ -202,6 +202,8 @@ struct AttnArgs {
     int64_t *o_acc;
     int trigger_tiles;   // k_attn: let the next kernel launch at the start when the row's context exceeds
                          // this many 64-position tiles, else once PV is done
+    int split_o;         // with o_w on 8-CTA clusters: the k_attn<C, true> variant (O slice in a buffer of
+                         // its own from the start, no head-output exchange; LLMX_ATTN_SPLIT_O)
     LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 
@@ -271,11 +273,14 @@ cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s);
 cudaError_t attn_configure(int max_smem_bytes, int cluster);
+// The split variant of the fused one-row kernel (8-CTA clusters): sets its shared
+// memory limit; *ok = 1 when every cluster of a grid of q_heads clusters fits at once.
+cudaError_t attn_split_configure(int smem_bytes, int q_heads, int *ok);
 // Blocks of several rows: one cluster per query head for all rows (K/V read once).
 cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s);
 cudaError_t attn_rows_configure(int max_smem_bytes, int cluster);
 size_t attn_rows_smem_bytes(int tpc, int cluster);
-size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows);
+size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows, bool split = false);
 cudaError_t launch_rmsnorm(const NormArgs &a, int rows, cudaStream_t s);
 cudaError_t launch_round_resid(const ResidArgs &a, int rows, cudaStream_t s);
 // carveout: preferred shared-memory carveout in percent for every projection

@@ -104,6 +104,9 @@ struct llmx_ctx {
     // one-row attention with the O projection fused (single GPU, LLMX_ATTN_FUSE_O):
     // the exact O sums [kMaxRows][hidden], finished by the next kernel's prologue
     bool fuse_o = true;
+    // the fused kernel's split variant (LLMX_ATTN_SPLIT_O=1; off by default):
+    // O slice copied from the start, no head-output exchange
+    bool attn_split_o = false;
     int64_t *o_acc = nullptr;
     // the O weights once more, head-major ([head][hidden rows][hd/2] words per
     // layer), so that a fused-attention CTA's slice is one contiguous copy
@@ -438,6 +441,7 @@ bool use_fuse_o(const llmx_ctx *c, uint32_t rows) {
 
 void set_fuse_o(llmx_ctx *c, AttnArgs &t, uint32_t layer) {
     t.o_w = c->o_heads + (size_t)layer * c->w_o;
+    t.split_o = c->attn_split_o ? 1 : 0;
     t.o_rows = c->s.hidden / t.cluster;
     t.hidden = c->s.hidden;
     t.o_acc = c->o_acc;
@@ -955,6 +959,15 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (c->fuse_o && dalloc(c, &c->o_heads, c->w_o * s.layers) != LLMX_OK) {
         c->fuse_o = false;
         (void)cudaGetLastError();
+    }
+    if (c->fuse_o && env_int("LLMX_ATTN_SPLIT_O", 0, 0, 1) == 1) {
+        int ok = 0;
+        const size_t b = attn_smem_bytes(c->tpc_max, hd, kCluster, (int)(H / kCluster), true);
+        if (attn_split_configure((int)b, c->hq, &ok) != cudaSuccess) {
+            ok = 0;
+            (void)cudaGetLastError();
+        }
+        c->attn_split_o = ok != 0;  // else the default kernel (every cluster must be resident at once)
     }
 
     // tensor-core projections for blocks of mma_min_rows..8 rows: QKV tiles are
