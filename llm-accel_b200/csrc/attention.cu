@@ -440,8 +440,14 @@ size_t attn_rows_smem_bytes(int tpc, int cluster) {
 }
 
 constexpr int kAttnRowsThreads = 256;
+constexpr int kRowGroup = 4;  // rows per thread in the row-inner loop order
 
-template <int C>
+// kRowInner (LLMX_ATTN_ROWS_INNER): QK and PV loop over a group of kRowGroup
+// rows innermost, so each K / V element is converted to Q4.12 and each K vector
+// loaded once per group instead of once per row.  The products, their banks
+// (element index mod 4 for QK, position mod 4 for PV) and the halves are those
+// of the row-outer order, so every sum is the same exact integer.
+template <int C, bool kRowInner>
 __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a) {
     LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(16) char raw[];
@@ -504,6 +510,51 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
 
     // ---- 1. scores of every (row, position) of the row's context -----------
     const int rot = (threadIdx.x & 31) % vpr;
+    if constexpr (kRowInner) {
+        const int groups = (R + kRowGroup - 1) / kRowGroup;
+        for (int i = threadIdx.x; i < groups * npos; i += blockDim.x) {
+            const int g = i / npos, pp = i - g * npos, r0 = g * kRowGroup;
+            const uint4 *kv = reinterpret_cast<const uint4 *>(m.kv + pp * hd);
+            int32_t b[kRowGroup][2][4];
+#pragma unroll
+            for (int rr = 0; rr < kRowGroup; rr++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) b[rr][0][j] = b[rr][1][j] = 0;
+            for (int e8 = 0; e8 < vpr; e8 += 2) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {  // half h: the row-outer loop's b[h] (vectors e8 + h)
+                    if (e8 + h >= vpr) break;
+                    const int v = rot_vec(e8 + h + rot, vpr);
+                    const uint4 k = kv[v];
+                    const int32_t kk[8] = {q412(lo16(k.x)), q412(hi16(k.x)), q412(lo16(k.y)), q412(hi16(k.y)),
+                                           q412(lo16(k.z)), q412(hi16(k.z)), q412(lo16(k.w)), q412(hi16(k.w))};
+#pragma unroll
+                    for (int rr = 0; rr < kRowGroup; rr++) {
+                        const uint4 q = reinterpret_cast<const uint4 *>(m.q + (r0 + rr) * kMaxHd)[v];
+                        b[rr][h][0] += qk_prod(lo16(q.x), kk[0]);
+                        b[rr][h][1] += qk_prod(hi16(q.x), kk[1]);
+                        b[rr][h][2] += qk_prod(lo16(q.y), kk[2]);
+                        b[rr][h][3] += qk_prod(hi16(q.y), kk[3]);
+                        b[rr][h][0] += qk_prod(lo16(q.z), kk[4]);
+                        b[rr][h][1] += qk_prod(hi16(q.z), kk[5]);
+                        b[rr][h][2] += qk_prod(lo16(q.w), kk[6]);
+                        b[rr][h][3] += qk_prod(hi16(q.w), kk[7]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int rr = 0; rr < kRowGroup; rr++) {
+                const int r = r0 + rr;
+                if (r >= R || pp >= npos_of(r)) continue;  // rows past the block: garbage q, never stored
+                int64_t t64 = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) t64 += sat32((int64_t)b[rr][0][j] + b[rr][1][j]);
+                int32_t tot = sat32(t64);
+                tot = sat32(rnd((int64_t)tot * a.qk_scale, 16));
+                m.sc[r * P + pp] = (int16_t)sat16(rnd(tot, 8));
+            }
+        }
+    } else
     for (int i = threadIdx.x; i < R * npos; i += blockDim.x) {
         const int r = i / npos, pp = i - r * npos;
         if (pp >= npos_of(r)) continue;
@@ -588,6 +639,45 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
             *cluster.map_shared_rank(m.gold + r * kMaxTiles + t, k) = old;
         }
     }
+    if constexpr (kRowInner) {
+        const int groups = (R + kRowGroup - 1) / kRowGroup;
+        for (int i = threadIdx.x; i < groups * nown * hd; i += blockDim.x) {
+            const int g = i / (nown * hd), rem = i - g * nown * hd, tli = rem / hd, e = rem - tli * hd;
+            const int r0 = g * kRowGroup, pb = tli * kTile;
+            int pe_r[kRowGroup], pe_max = pb;
+#pragma unroll
+            for (int rr = 0; rr < kRowGroup; rr++) {  // end of this tile in row r0 + rr's context
+                pe_r[rr] = r0 + rr < R ? min(pb + kTile, npos_of(r0 + rr)) : pb;
+                pe_max = max(pe_max, pe_r[rr]);
+            }
+            if (pe_max <= pb) continue;
+            int32_t bk[kRowGroup][4];
+#pragma unroll
+            for (int rr = 0; rr < kRowGroup; rr++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) bk[rr][j] = 0;
+            for (int p4 = pb; p4 < pe_max; p4 += 4) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {  // bank j: positions pb + j (mod 4), as in the row-outer loop
+                    const int pp = p4 + j;
+                    if (pp >= pe_max) break;
+                    const int32_t vv = q412(m.kv[pp * hd + e]);
+#pragma unroll
+                    for (int rr = 0; rr < kRowGroup; rr++)
+                        if (pp < pe_r[rr]) bk[rr][j] += qk_prod(m.sc[(r0 + rr) * P + pp], vv);
+                }
+            }
+#pragma unroll
+            for (int rr = 0; rr < kRowGroup; rr++) {
+                const int r = r0 + rr;
+                if (pe_r[rr] <= pb) continue;  // past the block, or the tile is beyond this row's context
+                int32_t ts = sat32((int64_t)bk[rr][0] + bk[rr][1] + bk[rr][2] + bk[rr][3]);
+                ts = sat32(rnd((int64_t)ts * 1024, 16));
+                const int16_t tv = (int16_t)sat16(rnd(ts, 8));
+                *cluster.map_shared_rank(m.tvr + (r * kMaxTiles + t_begin + tli) * epc + e / C, e % C) = tv;
+            }
+        }
+    } else
     for (int i = threadIdx.x; i < R * nown * hd; i += blockDim.x) {
         const int r = i / (nown * hd), rem = i - r * nown * hd, tli = rem / hd, e = rem - tli * hd;
         const int pb = tli * kTile, pe = min(pb + kTile, npos_of(r));
@@ -627,13 +717,23 @@ __global__ void __launch_bounds__(kAttnRowsThreads) k_attn_rows(const AttnArgs a
     }
 }
 
-cudaError_t attn_rows_configure(int max_smem_bytes, int cluster) {
+template <bool kRowInner>
+static cudaError_t attn_rows_configure_v(int max_smem_bytes, int cluster) {
     if (cluster == kClusterWide) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_rows<kClusterWide>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaError_t e = cudaFuncSetAttribute(k_attn_rows<kClusterWide, kRowInner>,
+                                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        return cudaFuncSetAttribute(k_attn_rows<kClusterWide>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+        return cudaFuncSetAttribute(k_attn_rows<kClusterWide, kRowInner>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    max_smem_bytes);
     }
-    return cudaFuncSetAttribute(k_attn_rows<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+    return cudaFuncSetAttribute(k_attn_rows<kCluster, kRowInner>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                max_smem_bytes);
+}
+
+cudaError_t attn_rows_configure(int max_smem_bytes, int cluster) {
+    cudaError_t e = attn_rows_configure_v<false>(max_smem_bytes, cluster);
+    if (e != cudaSuccess) return e;
+    return attn_rows_configure_v<true>(max_smem_bytes, cluster);
 }
 
 cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
@@ -654,7 +754,11 @@ cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn_rows<kClusterWide> : (const void *)k_attn_rows<kCluster>;
+    const bool wide = a.cluster == kClusterWide;
+    const void *fn = a.rows_inner ? (wide ? (const void *)k_attn_rows<kClusterWide, true>
+                                          : (const void *)k_attn_rows<kCluster, true>)
+                                  : (wide ? (const void *)k_attn_rows<kClusterWide, false>
+                                          : (const void *)k_attn_rows<kCluster, false>);
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

@@ -204,6 +204,7 @@ struct AttnArgs {
                          // this many 64-position tiles, else once PV is done
     int split_o;         // with o_w on 8-CTA clusters: the k_attn<C, true> variant (O slice in a buffer of
                          // its own from the start, no head-output exchange; LLMX_ATTN_SPLIT_O)
+    int rows_inner;      // k_attn_rows: the row-inner loop order (LLMX_ATTN_ROWS_INNER)
     LLMX_TL_FIELD        // timeline builds only: this launch's slot
 };
 

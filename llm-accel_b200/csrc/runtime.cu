@@ -107,6 +107,9 @@ struct llmx_ctx {
     // the fused kernel's split variant (LLMX_ATTN_SPLIT_O=1; off by default):
     // O slice copied from the start, no head-output exchange
     bool attn_split_o = false;
+    // blocks of several rows: the row-inner loop order of the rows kernel
+    // (LLMX_ATTN_ROWS_INNER=1; off by default)
+    bool attn_rows_inner = false;
     int64_t *o_acc = nullptr;
     // the O weights once more, head-major ([head][hidden rows][hd/2] words per
     // layer), so that a fused-attention CTA's slice is one contiguous copy
@@ -368,6 +371,7 @@ void pick_attn_cluster(const llmx_ctx *c, AttnArgs &t, uint32_t rows) {
 cudaError_t launch_attention(llmx_ctx *c, AttnArgs t, uint32_t rows) {
     if ((int)rows >= c->attn_rows_min) {
         t.pf_per_tile = 0;
+        t.rows_inner = c->attn_rows_inner ? 1 : 0;
         if (c->attn_rows_wide) {  // 16 CTAs per head: the block's rows multiply each CTA's work
             t.cluster = kClusterWide;
             t.tpc_max = c->tpc_max_wide;
@@ -906,6 +910,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (e == cudaSuccess) e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
     c->attn_rows_min = env_int("LLMX_ATTN_ROWS_MIN", 2, 2, 9);
+    c->attn_rows_inner = env_int("LLMX_ATTN_ROWS_INNER", 0, 0, 1) == 1;
     if (hd % kClusterWide == 0 && env_int("LLMX_ATTN_ROWS_WIDE", 0, 0, 1) == 1) {
         e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max_wide, kClusterWide), kClusterWide);
         if (e == cudaSuccess) c->attn_rows_wide = true;
