@@ -11,7 +11,9 @@ decodes from 2048).  Prefill tok/s of the prompt is reported beside it.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl llmx|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
 
-Rank 0 prints one JSON line.  `--impl reference` times the reference's
+Rank 0 prints one JSON line.  At N=1 it also carries `configs`: BASELINE
+configs 0-2 (one or two layers, the prefill-length sweep) as small bounded runs
+after the headline.  `--impl reference` times the reference's
 fixed-point oracle (its CPU restatement in oracle/, all host threads) on the
 same workload.
 """
@@ -335,6 +337,9 @@ def run_llmx(args, cfg_id, world, rank, local, K, W):
         result["generate"] = gen
     if cpu is not None:
         result["cpu_baseline"] = cpu
+    if world == 1 and not args.no_configs:  # BASELINE configs 0-2 beside the headline, on a free device
+        acc.close()
+        result["configs"] = config_legs()
     if rank == 0:
         emit(json.dumps(result))
     acc.close()
@@ -386,6 +391,147 @@ def generate_leg(acc, model, shape, prompt, device_time, stream, new_tokens=64):
             "lm_head_argmax_ms": am_ms, "lm_head_gbs": shape.vocab * shape.hidden * 2 / (am_ms * 1e-3) / 1e9,
             "host_lm_head_argmax_ms": host_ms, "host_threads": os.cpu_count(), "vocab_upload_s": upload_s,
             "api": "llmx_generate (device embedding gather + stack + LM-head argmax, one host wait)"}
+
+
+def config_legs():
+    """BASELINE configs 0-2 on one GPU, each a small bounded run beside the
+    headline (config 3), with the same synthetic model family (seeded N(0,0.02)
+    Q4.12 weights, N(0,1) Q8.8 embedding rows, norm weights 1.0):
+      config 0: one layer, a P8 block at position 0 then one decode row at 8,
+                through llmx_stack (host rows in, final-normed rows out), checked
+                against the oracle, which is also timed (1 thread);
+      config 1: two layers, P8/G2: the prompt block and one decode through the
+                executor (run_prompt_block / run_token) with the untied
+                151,936-row LM head argmax on the host, and the same two tokens
+                from llmx_generate (argmax on the device);
+      config 2: one layer, a 1024-token prompt as 128 consecutive P8 blocks with
+                the KV cache built by the device: prefill tok/s after 8, 64,
+                256 and 1024 tokens (CUDA events on the context stream).
+    A failure is reported in the returned object, never raised."""
+    import torch
+    import llmx
+
+    out = {}
+    reps = 50
+    O = _oracle()
+    from helpers import OracleState, oracle_shape
+
+    def e2e_ms(fn):
+        fn()  # warm-up: graph capture
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) * 1e3 / reps
+
+    # ---- config 0
+    try:
+        s = llmx.shape("qwen2.5-3b", layers=1, max_seq=64)
+        m = llmx.Model(s).init_gaussian(SEED, W_SIGMA)
+        acc = llmx.Accelerator(s)
+        try:
+            acc.upload_model(m)
+            rows = embed_rows(range(9), s.hidden).astype(np.int16)
+            got_p, got_d = acc.stack(rows[:8], position=0), acc.stack(rows[8:9], position=8)
+            O.set_threads(1)
+            ref = OracleState(O, oracle_shape(O, s), [m.layer(0)], m.norms())
+            t0 = time.perf_counter()
+            want_p = ref.stack(rows[:8], 0)
+            t1 = time.perf_counter()
+            want_d = ref.stack(rows[8:9], 8)
+            t2 = time.perf_counter()
+            p8_ms = e2e_ms(lambda: acc.stack(rows[:8], position=0))
+            dec_ms = e2e_ms(lambda: acc.stack(rows[8:9], position=8))
+            out["config0"] = {
+                "workload": "1 Qwen2.5-3B-shaped layer: P8 block at position 0, then one decode row at position 8",
+                "p8_block_ms": p8_ms, "decode_ms": dec_ms, "prefill_tok_s": 8 / (p8_ms * 1e-3),
+                "decode_tok_s": 1 / (dec_ms * 1e-3),
+                "matches_oracle": bool(np.array_equal(got_p, want_p) and np.array_equal(got_d, want_d)),
+                "cpu_oracle_ms": {"p8_block": (t1 - t0) * 1e3, "decode": (t2 - t1) * 1e3, "cores": 1},
+                "timing": f"llmx_stack end to end (host rows, H2D, graph, D2H), mean of {reps} calls"}
+        finally:
+            acc.close()
+    except Exception as e:  # reported, not raised: the headline line must print
+        out["config0"] = {"error": f"{type(e).__name__}: {e}"}
+
+    # ---- config 1
+    try:
+        s = llmx.shape("qwen2.5-3b", layers=2, max_seq=64)
+        m = llmx.Model(s).init_gaussian(SEED, W_SIGMA, lm_head=True)
+        acc = llmx.Accelerator(s)
+        try:
+            acc.upload_model(m)
+            ex = llmx.Executor(acc, m)
+            prompt = list(range(8))
+
+            def host_path():
+                t0 = time.perf_counter()
+                r = ex.run_prompt_block(prompt, 0)
+                t1 = time.perf_counter()
+                a = m.lm_head_argmax(r[-1])
+                t2 = time.perf_counter()
+                d = ex.run_token(a, 8)
+                t3 = time.perf_counter()
+                b = m.lm_head_argmax(d[0])
+                t4 = time.perf_counter()
+                return [a, b], (t1 - t0 + t3 - t2) * 1e3, (t2 - t1 + t4 - t3) * 1e3
+
+            host_path()  # warm-up
+            toks, fwd_ms, head_ms = host_path()
+            acc.upload_vocab(m)
+            acc.reset_kv()
+            dev = acc.generate(prompt, 2)
+            t0 = time.perf_counter()
+            dev = acc.generate(prompt, 2)
+            gen_ms = (time.perf_counter() - t0) * 1e3
+            out["config1"] = {
+                "workload": "2 Qwen2.5-3B-shaped layers, P8/G2: prompt tokens 0..7 in one block, one decode; "
+                            "untied N(0,0.02) 151,936 x 2048 LM head",
+                "generated": toks, "device_generated": dev, "device_matches_host": toks == dev,
+                "host_path_ms": fwd_ms + head_ms, "forward_ms": fwd_ms, "host_lm_head_ms": head_ms,
+                "host_threads": os.cpu_count(), "device_generate_ms": gen_ms,
+                "timing": "wall clock of one warm call (executor + host argmax; llmx_generate)"}
+        finally:
+            acc.close()
+    except Exception as e:
+        out["config1"] = {"error": f"{type(e).__name__}: {e}"}
+
+    # ---- config 2
+    try:
+        s = llmx.shape("qwen2.5-3b", layers=1, max_seq=1024)
+        m = llmx.Model(s).init_gaussian(SEED, W_SIGMA)
+        acc = llmx.Accelerator(s)
+        try:
+            acc.upload_model(m)
+            stream = torch.cuda.ExternalStream(acc.stream)
+            marks = (8, 64, 256, 1024)
+
+            def sweep(events):
+                for b in range(128):
+                    acc.stack_async(8, 0, 1, 8 * b, include_final_norm=False)
+                    if 8 * (b + 1) in events:
+                        events[8 * (b + 1)].record(stream)
+
+            acc.write_hidden(1, embed_rows(range(8), s.hidden).astype(np.int16))
+            sweep({})  # warm-up: graph capture
+            acc.synchronize()
+            acc.reset_kv()
+            e0 = torch.cuda.Event(enable_timing=True)
+            ev = {n: torch.cuda.Event(enable_timing=True) for n in marks}
+            e0.record(stream)
+            sweep(ev)
+            ev[marks[-1]].synchronize()
+            acc.synchronize()
+            out["config2"] = {
+                "workload": "1 Qwen2.5-3B-shaped layer, prompts of 8/64/256/1024 tokens as consecutive P8 blocks, "
+                            "causal KV cache built by the device",
+                "prefill_tok_s": {str(n): n / (e0.elapsed_time(ev[n]) * 1e-3) for n in marks},
+                "ms": {str(n): e0.elapsed_time(ev[n]) for n in marks},
+                "timing": "CUDA events on the context stream around consecutive llmx_stack_async blocks"}
+        finally:
+            acc.close()
+    except Exception as e:
+        out["config2"] = {"error": f"{type(e).__name__}: {e}"}
+    return out
 
 
 def _oracle():
@@ -552,6 +698,7 @@ def main():
     ap.add_argument("--impl", choices=["llmx", "reference"], default="llmx")
     ap.add_argument("--config", type=int, choices=[3, 4], default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE config 0-2 legs (N=1)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
