@@ -122,7 +122,12 @@ size_t attn_smem_bytes(int tpc, int hd, int cluster, int o_rows, bool split) {
 // into a buffer of its own from the kernel's start, and the PV tile values go
 // to every CTA, which then runs the recurrence of all hd elements itself -- no
 // third cluster barrier (the head-output exchange) before the O rows.
-template <int C, bool kSplit>
+// kTp (O projection fused on a tensor-parallel rank, LLMX_ATTN_FUSE_O_TP): the
+// rank's O sums of a slice of O rows are complete once the CTA of that slice of
+// every local head has added its part; the last of them to arrive pushes the
+// slice to every rank's exchange region (the words the O projection's
+// EPI_PARTIAL epilogue would store) and clears the sums and the count.
+template <int C, bool kSplit, bool kTp>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     LLMX_TL_GUARD(a.tl_slot);
     extern __shared__ __align__(16) char raw[];
@@ -395,6 +400,28 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
         const int64_t tot = (int64_t)hi * 256 + lo;
         atomicAdd(reinterpret_cast<unsigned long long *>(a.o_acc + (size_t)r * a.hidden + (size_t)c * a.o_rows + j),
                   (unsigned long long)tot);
+    }
+    if constexpr (kTp) {
+        __shared__ int last_s;
+        __syncthreads();  // every atomic of this CTA issued
+        if (threadIdx.x == 0) {
+            __threadfence();  // ... and visible before the arrival is counted
+            int *cnt = a.o_cnt + r * C + c;
+            last_s = atomicAdd(cnt, 1) == a.q_heads - 1;
+            if (last_s) *cnt = 0;  // next used by the next layer's launch
+        }
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();
+        const uint32_t n = st.ar_base + a.ar_off;
+        for (int j = threadIdx.x; j < a.o_rows; j += blockDim.x) {
+            const int row = c * a.o_rows + j;
+            const int64_t v = (int64_t)atomicExch(
+                reinterpret_cast<unsigned long long *>(a.o_acc + (size_t)r * a.hidden + row), 0ull);
+            const size_t w = ar_word_index((int)(n & 1u), a.ar.me, r, a.ar.hidden, row);
+            const uint64_t word = ar_pack(v, ar_tag(n));
+            for (int q = 0; q < a.ar.n; q++) ar_store(reinterpret_cast<uint64_t *>(a.ar.base[q] + kArHeader) + w, word);
+        }
     }
 }
 
@@ -762,21 +789,29 @@ cudaError_t launch_attn_rows(const AttnArgs &a, cudaStream_t s) {
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-cudaError_t attn_configure(int max_smem_bytes, int cluster) {
+template <bool kTp>
+static cudaError_t attn_configure_v(int max_smem_bytes, int cluster) {
     if (cluster == kClusterWide) {
         cudaError_t e =
-            cudaFuncSetAttribute(k_attn<kClusterWide, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            cudaFuncSetAttribute(k_attn<kClusterWide, false, kTp>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        return cudaFuncSetAttribute(k_attn<kClusterWide, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        return cudaFuncSetAttribute(k_attn<kClusterWide, false, kTp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     max_smem_bytes);
     }
-    return cudaFuncSetAttribute(k_attn<kCluster, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
+    return cudaFuncSetAttribute(k_attn<kCluster, false, kTp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                max_smem_bytes);
+}
+
+cudaError_t attn_configure(int max_smem_bytes, int cluster, bool tp) {
+    cudaError_t e = attn_configure_v<false>(max_smem_bytes, cluster);
+    if (e == cudaSuccess && tp) e = attn_configure_v<true>(max_smem_bytes, cluster);
+    return e;
 }
 
 cudaError_t attn_split_configure(int smem_bytes, int q_heads, int *ok) {
     *ok = 0;
     cudaError_t e =
-        cudaFuncSetAttribute(k_attn<kCluster, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        cudaFuncSetAttribute(k_attn<kCluster, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
     if (e != cudaSuccess) return e;
     // every cluster of the one-row grid must be resident at once
     cudaLaunchConfig_t cfg = {};
@@ -791,7 +826,7 @@ cudaError_t attn_split_configure(int smem_bytes, int q_heads, int *ok) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, (const void *)k_attn<kCluster, true>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&clusters, (const void *)k_attn<kCluster, true, false>, &cfg);
     if (e != cudaSuccess) return e;
     *ok = clusters >= q_heads ? 1 : 0;
     return cudaSuccess;
@@ -804,8 +839,10 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.cluster * a.q_heads, rows);
     cfg.blockDim = dim3(kAttnThreads);
-    // the split variant only for the fused O projection on 8-CTA clusters
-    const bool split = a.split_o && a.o_w != nullptr && a.cluster == kCluster;
+    // the push to the peers only with the fused O projection on a tensor-parallel
+    // rank; the split variant only for the fused O projection of one GPU on 8-CTA clusters
+    const bool tp = a.o_w != nullptr && a.ar.n > 1;
+    const bool split = !tp && a.split_o && a.o_w != nullptr && a.cluster == kCluster;
     cfg.dynamicSmemBytes = attn_smem_bytes(a.tpc_max, a.hd, a.cluster, a.o_w != nullptr ? a.o_rows : 0, split);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -817,9 +854,12 @@ cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const void *fn = a.cluster == kClusterWide ? (const void *)k_attn<kClusterWide, false>
-                     : split                      ? (const void *)k_attn<kCluster, true>
-                                                  : (const void *)k_attn<kCluster, false>;
+    const bool wide = a.cluster == kClusterWide;
+    const void *fn = tp      ? (wide ? (const void *)k_attn<kClusterWide, false, true>
+                                     : (const void *)k_attn<kCluster, false, true>)
+                     : wide  ? (const void *)k_attn<kClusterWide, false, false>
+                     : split ? (const void *)k_attn<kCluster, true, false>
+                             : (const void *)k_attn<kCluster, false, false>;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

@@ -202,6 +202,12 @@ struct AttnArgs {
     int64_t *o_acc;
     int trigger_tiles;   // k_attn: let the next kernel launch at the start when the row's context exceeds
                          // this many 64-position tiles, else once PV is done
+    // fused O on a tensor-parallel rank (k_attn<C, *, true>, LLMX_ATTN_FUSE_O_TP): the rank's exact O sums
+    // go to every rank's exchange region as all-reduce number step->ar_base + ar_off, pushed by the last
+    // of the rank's heads to finish each slice of O rows (arrivals counted in o_cnt[row][cluster CTA])
+    ArPeers ar;
+    uint32_t ar_off;
+    int *o_cnt;
     int split_o;         // with o_w on 8-CTA clusters: the k_attn<C, true> variant (O slice in a buffer of
                          // its own from the start, no head-output exchange; LLMX_ATTN_SPLIT_O)
     int rows_inner;      // k_attn_rows: the row-inner loop order (LLMX_ATTN_ROWS_INNER)
@@ -273,7 +279,8 @@ cudaError_t launch_ar_finish(const ArFinishArgs &a, cudaStream_t s);
 // Launchers (stream-ordered, programmatic-dependent launch enabled).
 cudaError_t launch_proj(const ProjArgs &a, int epi, int rows_tmpl, int grid, cudaStream_t s);
 cudaError_t launch_attn(const AttnArgs &a, int rows, cudaStream_t s);
-cudaError_t attn_configure(int max_smem_bytes, int cluster);
+// tp: also the tensor-parallel fused-O instantiations (LLMX_ATTN_FUSE_O_TP)
+cudaError_t attn_configure(int max_smem_bytes, int cluster, bool tp = false);
 // The split variant of the fused one-row kernel (8-CTA clusters): sets its shared
 // memory limit; *ok = 1 when every cluster of a grid of q_heads clusters fits at once.
 cudaError_t attn_split_configure(int smem_bytes, int q_heads, int *ok);

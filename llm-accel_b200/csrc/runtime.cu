@@ -107,6 +107,11 @@ struct llmx_ctx {
     // the fused kernel's split variant (LLMX_ATTN_SPLIT_O=1; off by default):
     // O slice copied from the start, no head-output exchange
     bool attn_split_o = false;
+    // tensor-parallel ranks: O fused into one-row attention with the peer push
+    // (LLMX_ATTN_FUSE_O_TP=1; off by default); o_cnt counts the heads done per
+    // [row][cluster CTA] slice of O rows
+    bool fuse_o_tp = false;
+    int *o_cnt = nullptr;
     // blocks of several rows: the row-inner loop order of the rows kernel
     // (LLMX_ATTN_ROWS_INNER=1; off by default)
     bool attn_rows_inner = false;
@@ -438,7 +443,8 @@ bool use_mma(const llmx_ctx *c, uint32_t rows, int proj) {
 }
 
 bool use_fuse_o(const llmx_ctx *c, uint32_t rows) {
-    return c->fuse_o && c->size == 1 && rows == 1 && (int)rows < c->attn_rows_min && c->s.hidden % kClusterWide == 0 &&
+    // tensor parallel: only with the peer all-reduce (the NCCL path reduces the O projection's partials)
+    return c->fuse_o && (c->size == 1 || c->ar.n > 1) && rows == 1 && (int)rows < c->attn_rows_min && c->s.hidden % kClusterWide == 0 &&
            !use_mma(c, rows, MP_GU) &&
            !use_mma(c, rows, MP_D);
 }
@@ -578,6 +584,14 @@ int enqueue_task(llmx_ctx *c, uint32_t op, uint32_t layer, uint32_t rows, uint32
         AttnArgs t = attn_args(c, layer);
         if (use_fuse_o(c, rows)) {  // O inside attention; the next prologue (or a finisher) rounds
             set_fuse_o(c, t, layer);
+            if (c->size > 1) {  // the last head of each O-row slice pushes the rank's sums to every rank
+                t.ar = c->ar;
+                t.ar_off = ar_next;
+                t.o_cnt = c->o_cnt;
+                CK(launch_attention(c, t, rows));
+                c->launches += 2;
+                return after_partial(c, rows, ar_next, out, in, fuse, pend);
+            }
             CK(launch_attention(c, t, rows));
             c->launches += 2;
             if (fuse) {
@@ -673,8 +687,9 @@ int set_step(llmx_ctx *c, uint32_t position, uint32_t rows) {
 int report_device_error(llmx_ctx *c, int v) {
     if (v != 0) {
         CK(cudaMemset(c->err, 0, sizeof(int)));
-        // a call that stopped part-way may leave fused-O sums behind
+        // a call that stopped part-way may leave fused-O sums (and head counts) behind
         CK(cudaMemset(c->o_acc, 0, sizeof(int64_t) * kMaxRows * c->s.hidden));
+        if (c->o_cnt) CK(cudaMemset(c->o_cnt, 0, sizeof(int) * kMaxRows * kClusterWide));
         if (v == kErrTokenRange) {
             g_last_error = "a token id reached the embedding gather outside the vocabulary";
             return LLMX_ERR_RANGE;
@@ -891,7 +906,8 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     c->gemv_warps = env_int("LLMX_GEMV_WARPS", 16, 2, 16);
     c->proj_carveout = env_int("LLMX_PROJ_CARVEOUT", 100, -1, 100);
     c->ar_fuse_rows = env_int("LLMX_AR_FUSE_ROWS", 2, 0, 8);
-    c->fuse_o = env_int("LLMX_ATTN_FUSE_O", 1, 0, 1) == 1 && c->size == 1;
+    c->fuse_o_tp = c->size > 1 && env_int("LLMX_ATTN_FUSE_O_TP", 0, 0, 1) == 1;
+    c->fuse_o = env_int("LLMX_ATTN_FUSE_O", 1, 0, 1) == 1 && (c->size == 1 || c->fuse_o_tp);
     auto bail = [&](int code) {
         release(c);
         return code;
@@ -906,7 +922,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (e != cudaSuccess) return bail(fail_cuda(e, "cudaStreamCreate"));
     e = proj_configure(kProjSmem, c->proj_carveout);
     if (e != cudaSuccess) return bail(fail_cuda(e, "proj_configure"));
-    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster, s.hidden / kCluster), kCluster);
+    e = attn_configure((int)attn_smem_bytes(c->tpc_max, hd, kCluster, s.hidden / kCluster), kCluster, c->fuse_o_tp);
     if (e == cudaSuccess) e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max, kCluster), kCluster);
     if (e != cudaSuccess) return bail(fail_cuda(e, "attn_configure"));
     c->attn_rows_min = env_int("LLMX_ATTN_ROWS_MIN", 2, 2, 9);
@@ -925,7 +941,7 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
     if (max_tiles > 2 * kCluster && hd % kClusterWide == 0 && c->attn_wide_div * c->hq * kClusterWide <= c->nsm &&
         wide_env >= 1) {
         e = attn_configure((int)attn_smem_bytes(c->tpc_max_wide, hd, kClusterWide, s.hidden / kClusterWide),
-                           kClusterWide);
+                           kClusterWide, c->fuse_o_tp);
         if (e == cudaSuccess)
             e = attn_rows_configure((int)attn_rows_smem_bytes(c->tpc_max_wide, kClusterWide), kClusterWide);
         if (e == cudaSuccess) c->attn_wide = true;
@@ -965,7 +981,9 @@ int llmx_create(const llmx_shape *shape, int device, int tp_rank, int tp_size, c
         c->fuse_o = false;
         (void)cudaGetLastError();
     }
-    if (c->fuse_o && env_int("LLMX_ATTN_SPLIT_O", 0, 0, 1) == 1) {
+    if (c->fuse_o && c->size > 1 && (rc = dalloc(c, &c->o_cnt, (size_t)kMaxRows * kClusterWide)))
+        return bail(rc);
+    if (c->fuse_o && c->size == 1 && env_int("LLMX_ATTN_SPLIT_O", 0, 0, 1) == 1) {
         int ok = 0;
         const size_t b = attn_smem_bytes(c->tpc_max, hd, kCluster, (int)(H / kCluster), true);
         if (attn_split_configure((int)b, c->hq, &ok) != cudaSuccess) {
