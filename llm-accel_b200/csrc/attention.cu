@@ -404,15 +404,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const AttnArgs a) {
     if constexpr (kTp) {
         __shared__ int last_s;
         __syncthreads();  // every atomic of this CTA issued
-        if (threadIdx.x == 0) {
-            __threadfence();  // ... and visible before the arrival is counted
-            int *cnt = a.o_cnt + r * C + c;
-            last_s = atomicAdd(cnt, 1) == a.q_heads - 1;
+        if (threadIdx.x == 0) {  // release this CTA's sums / acquire the other heads' (as the stream-K tiles)
+            int *cnt = a.o_cnt + r * C + c, old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+            last_s = old == a.q_heads - 1;
             if (last_s) *cnt = 0;  // next used by the next layer's launch
         }
         __syncthreads();
         if (!last_s) return;
-        __threadfence();
         const uint32_t n = st.ar_base + a.ar_off;
         for (int j = threadIdx.x; j < a.o_rows; j += blockDim.x) {
             const int row = c * a.o_rows + j;
